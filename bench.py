@@ -1,0 +1,423 @@
+"""Benchmark of the fused Local Attender (the UPLiFT hot path) on B200.
+
+Workload ("dinov2-s14-448-iters4"): the four Local Attender calls of the
+DINOv2-S/14 upsampler at 448 px, iters=4, B=8 images per GPU, bf16:
+value 384ch 32^2 -> 64^2 -> 128^2 -> 256^2 -> 512^2 under 64-ch guides,
+K=17, each call's output the next call's value.  One step = those four
+calls (2.785 output Mpix per GPU).  Synthetic inputs (seed 0, N(0,1)) and a
+random-init LocalAttender(64, 17) in bf16.  Inputs are larger than L2
+(3.0 GB streamed per step), so no L2 flush is needed between steps.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Prints one JSON line (rank 0).  `value` = output Mpix/s over all ranks with
+inputs resident in HBM (device time, max over ranks); `e2e` = the same
+metric through LocalAttender.forward with pinned host buffers and the
+host<->device copies inside the timed region; `roofline` = algorithmic
+HBM bytes / kernel time of the attender kernel vs the measured copy
+bandwidth; `cpu_baseline` = the reference algorithm (oracle port, torch
+CPU ops) on the host cores on a bounded sample.  Multi-GPU: weak scaling,
+each rank runs its own 8 images; no collective on the data path.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Local Attender output Mpix/s (bf16, DINOv2-S/14 448px iters=4 attender chain)"
+UNIT = "Mpix/s"
+K_NBR = 17
+CG = 64
+C = 384
+B_PER_GPU = 8
+LEVELS = [(32, 64), (64, 128), (128, 256), (256, 512)]  # (coarse, fine) sides
+ELEM = 2  # bf16 bytes
+
+
+def algo_bytes_per_pixel(Cg=CG, Cv=C, I=2, s=ELEM):
+    """guide read + output write + value read once (amortised over I^2)."""
+    return Cg * s + Cv * s + Cv * s / (I * I)
+
+
+def out_pixels(B=B_PER_GPU):
+    return sum(B * fo * fo for _, fo in LEVELS)
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    """DRAM bytes per step from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "la_fwd_dinov2_448_b8_traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_step:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device(f"cuda:{local}"))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_inputs(dev, B=B_PER_GPU, seed=0):
+    """Guides for the four levels and the level-0 value map (bf16, NHWC)."""
+    from uplift_b200.attender import LocalAttender
+    g = torch.Generator().manual_seed(seed)
+    torch.manual_seed(seed)
+    la = LocalAttender(CG, K_NBR).to(torch.bfloat16)  # default nn.Conv2d init under seed 0
+    value0 = torch.randn(B, C, LEVELS[0][0], LEVELS[0][0], generator=g).to(torch.bfloat16)
+    guides = [torch.randn(B, CG, fo, fo, generator=g).to(torch.bfloat16) for _, fo in LEVELS]
+    cl = torch.channels_last
+    host = dict(value0=value0.contiguous(memory_format=cl), guides=[x.contiguous(memory_format=cl) for x in guides])
+    return la, host
+
+
+def run_ours(args, world, rank, local):
+    from uplift_b200 import _native, ops
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    _native.load()
+    la, host = make_inputs(torch.device("cpu"), seed=0)
+    la = la.to(dev)
+    value0 = host["value0"].to(dev)
+    guides = [x.to(dev) for x in host["guides"]]
+    w = la.conv1.weight.detach().float().reshape(K_NBR, CG).contiguous()
+    b = la.conv1.bias.detach().float().contiguous()
+    offsets, pn = la.offsets, la.pn
+    outs = [torch.empty((B_PER_GPU, C, fo, fo), dtype=torch.bfloat16, device=dev,
+                        memory_format=torch.channels_last) for _, fo in LEVELS]
+    stream = torch.cuda.current_stream(dev)
+
+    def step(events=None):
+        v = value0
+        for i, g in enumerate(guides):
+            if events is not None:
+                events[i][0].record(stream)
+            ops.local_attender_raw(g, v, w, b, offsets, pn, out=outs[i])
+            if events is not None:
+                events[i][1].record(stream)
+            v = outs[i]
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    # ---- device-resident timing: K steps between a barrier + sync on both sides
+    clocks = ClockSampler(local)
+    clocks.start()
+    per_launch = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in LEVELS] for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for s in range(args.steps):
+        step(per_launch[s])
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clk = clocks.stop()
+    ms_local = t0.elapsed_time(t1)
+    kern_ms = [sum(per_launch[s][i][0].elapsed_time(per_launch[s][i][1]) for s in range(args.steps))
+               for i in range(len(LEVELS))]
+    ms_total = max_over_ranks(ms_local, world, dev)
+    ms_step = ms_total / args.steps
+    mpix_step = out_pixels() / 1e6
+    value = world * mpix_step / (ms_step / 1e3)
+
+    # ---- roofline of the attender kernel (all four launches of a step)
+    bpp = algo_bytes_per_pixel()
+    algo_bytes_step = out_pixels() * bpp
+    kern_ms_step = sum(kern_ms) / args.steps
+    achieved = algo_bytes_step / (kern_ms_step / 1e3) / 1e9
+    peak, peak_kind = load_peaks()
+    traffic = load_traffic()
+
+    # ---- end to end through the public module with pinned host buffers
+    e2e = None if args.no_e2e else run_e2e(la, host, dev, stream, world, args, mpix_step)
+
+    # ---- CPU baseline (rank 0, N=1 only): reference algorithm on host cores
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(la, host)
+
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seed 0, N(0,1) guides/values, random-init LocalAttender(64,17) in bf16)",
+        "config": {"workload": "dinov2-s14-448-iters4 Local Attender chain",
+                   "images_per_gpu": B_PER_GPU, "global_images": B_PER_GPU * world,
+                   "K": K_NBR, "guide_channels": CG, "value_channels": C, "scale": 2,
+                   "levels": [f"{c}^2->{f}^2" for c, f in LEVELS],
+                   "out_mpix_per_step_per_gpu": round(mpix_step, 4),
+                   "l2": "inputs larger than L2 (3.03 GB algorithmic per step), no flush",
+                   "parallelism": f"batch-sharded x{world}, no data-path collective"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": traffic, "algo_bytes_per_step": algo_bytes_step,
+                     "algo_bytes_per_pixel": bpp,
+                     "kernel_ms_per_level": [round(x / args.steps, 4) for x in kern_ms]},
+        "e2e": e2e,
+        "gpu_launches": len(LEVELS) * args.steps,
+        "clocks": clk,
+    }
+    if cpu is not None:
+        result["cpu_baseline"] = cpu
+    return result
+
+
+def run_e2e(la, host, dev, stream, world, args, mpix_step):
+    """The same metric through LocalAttender.forward: every step copies the
+    level-0 features and the four guides from pinned host memory, runs the
+    four attender calls and copies the final output back to pinned host
+    memory, all inside the timed region."""
+    h_v0 = host["value0"].pin_memory()
+    h_guides = [x.pin_memory() for x in host["guides"]]
+    h_out = torch.empty((B_PER_GPU, C, LEVELS[-1][1], LEVELS[-1][1]), dtype=torch.bfloat16,
+                        memory_format=torch.channels_last).pin_memory()
+    h2d = h_v0.numel() * 2 + sum(x.numel() * 2 for x in h_guides)
+    d2h = h_out.numel() * 2
+
+    def e2e_step():
+        v = h_v0.to(dev, non_blocking=True)
+        for hg in h_guides:
+            v = la(hg.to(dev, non_blocking=True), v)
+        h_out.copy_(v, non_blocking=True)
+
+    with torch.inference_mode():
+        for _ in range(max(1, min(args.warmup, 3))):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        e_steps = max(1, min(args.steps, 10))
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+    e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / e_steps
+    return {"value": round(world * mpix_step / (e_ms / 1e3), 2), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms, 3),
+            "api": "uplift_b200.LocalAttender.forward, pinned host buffers"}
+
+
+def cpu_sample_inputs(host, seed=1):
+    """Per level: the guide and a value map of one image (level 0: the real
+    level-0 features; deeper levels: synthetic N(0,1) maps of the shape the
+    chain would feed them)."""
+    g = torch.Generator().manual_seed(seed)
+    vals = [host["value0"][:1].contiguous()]
+    for c, _ in LEVELS[1:]:
+        vals.append(torch.randn(1, C, c, c, generator=g).to(torch.bfloat16))
+    return [(host["guides"][i][:1].contiguous(), vals[i]) for i in range(len(LEVELS))]
+
+
+def cpu_band_step(la, inputs, band):
+    """Reference algorithm (the oracle's restatement of the non-fast
+    LocalAttender with torch CPU ops, parallel pooling, bf16) on band `band`
+    of 8 horizontal bands of every level of one image; each band is computed
+    with its +-pn halo rows, so its output equals the whole-image result.
+    Returns the output pixels produced."""
+    from oracle import local_attender_oracle as lao
+    w = la.conv1.weight.detach().cpu().reshape(K_NBR, CG)
+    b = la.conv1.bias.detach().cpu()
+    pn = la.pn
+    pix = 0
+    with torch.inference_mode():
+        for (guide, value) in inputs:
+            H = value.shape[2]
+            h0, h1 = band * H // 8, (band + 1) * H // 8
+            lo, hi = max(0, h0 - pn), min(H, h1 + pn)
+            lao.local_attender(guide[:, :, 2 * lo:2 * hi], value[:, :, lo:hi], w, b, K=K_NBR)
+            pix += 2 * (h1 - h0) * guide.shape[3]
+    return pix
+
+
+def cpu_baseline(la, host, min_seconds=10.0):
+    """Rank 0, N=1: bands 0..7 (= one whole image of the 4-level chain),
+    repeated until about `min_seconds` of CPU work, all host threads."""
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    inputs = cpu_sample_inputs(host)
+    cpu_band_step(la, inputs, 4)  # warm-up
+    t = time.perf_counter()
+    pix, n = 0, 0
+    while True:
+        pix += cpu_band_step(la, inputs, n % 8)
+        n += 1
+        sec = time.perf_counter() - t
+        if n >= 8 and sec >= min_seconds:
+            break
+    return {"value": round(pix / 1e6 / sec, 4), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{n} bands of 1/8 image rows x 4 attender levels (= {n / 8:.2f} images of "
+                      f"the 448px iters=4 chain, {pix} output px) in {sec:.1f} s; reference "
+                      "algorithm restated with torch CPU ops (parallel pooling), bf16"}
+
+
+def run_reference(args, world, rank):
+    """The reference's CPU implementation of the path (oracle port), rank 0.
+    One step = one 1/8-row band of one image through the 4 attender levels."""
+    if rank != 0:
+        return None
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    la, host = make_inputs(torch.device("cpu"), seed=0)
+    inputs = cpu_sample_inputs(host)
+    for i in range(min(args.warmup, 2)):
+        cpu_band_step(la, inputs, i % 8)
+    pix = 0
+    t = time.perf_counter()
+    for i in range(args.steps):
+        pix += cpu_band_step(la, inputs, i % 8)
+    sec = time.perf_counter() - t
+    value = pix / 1e6 / sec
+    sample = (f"per step 1/8 of the rows of one image through the 4 attender levels "
+              f"({pix // max(args.steps, 1)} output px avg), reference algorithm restated with torch "
+              "CPU ops (parallel pooling), bf16")
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(sec * 1e3 / max(args.steps, 1), 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "dinov2-s14-448-iters4 Local Attender chain", "K": K_NBR,
+                       "guide_channels": CG, "value_channels": C, "scale": 2},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    global B_PER_GPU
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end pass")
+    ap.add_argument("--images", type=int, default=8,
+                    help="images per GPU (default 8; smaller only for profiling captures)")
+    args = ap.parse_args()
+    B_PER_GPU = args.images
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, world, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    world, rank, local = dist_setup()
+    try:
+        res = run_ours(args, world, rank, local)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,112 @@
+/*
+ * uplift_la.h -- C ABI of the B200 (sm_100a) UPLiFT Local Attender.
+ *
+ * The Local Attender upsamples a coarse "value" map [B, C, H, W] to
+ * [B, C, I*H, I*W] under the guidance of a fine "guide" map
+ * [B, Cg, I*H, I*W].  For every output pixel (y, x) with parent coarse cell
+ * (h, w) = (y / I, x / I) it computes
+ *
+ *     logit[k] = bias[k] + sum_c weight[k][c] * guide[c, y, x]
+ *                (+ guide[k, y, x] for k < min(K, Cg) when conv_res)
+ *     p        = softmax_k(logit)          (one-hot of the first argmax when hardmax)
+ *     out[c, y, x] = sum_k p[k] * value[c, clamp(h + dy[k]), clamp(w + dx[k])]
+ *
+ * where clamp() to [0, H-1] / [0, W-1] is the replicate padding of the
+ * reference.  All arithmetic is fp32; tensors are stored as fp32, bf16 or
+ * fp16 (all three of guide / value / out in the same type).
+ *
+ * Tensors are described by a base pointer and four element strides in the
+ * logical order [B, channel, row, col].  The channel stride must be 1
+ * (channels_last / NHWC storage, which is what the fast path of the
+ * reference uses); other strides are free (sliced or padded tensors work).
+ * All pointers are device pointers of the current CUDA device unless noted.
+ *
+ * No entry point allocates device memory, synchronises the stream or aborts
+ * the process: each returns UPLIFT_LA_OK or an error code, and
+ * uplift_la_last_error() gives a message for the calling thread.
+ */
+#ifndef UPLIFT_LA_H_
+#define UPLIFT_LA_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* storage types (guide, value, logits and out share one) */
+#define UPLIFT_LA_F32  0
+#define UPLIFT_LA_BF16 1
+#define UPLIFT_LA_F16  2
+
+/* status codes */
+#define UPLIFT_LA_OK             0
+#define UPLIFT_LA_ERR_ARG        1  /* null pointer, bad enum value         */
+#define UPLIFT_LA_ERR_SHAPE      2  /* sizes inconsistent or unsupported    */
+#define UPLIFT_LA_ERR_LAYOUT     3  /* channel stride != 1, misalignment    */
+#define UPLIFT_LA_ERR_OFFSETS    4  /* |offset| > pn, or pn out of range    */
+#define UPLIFT_LA_ERR_CUDA       5  /* a CUDA runtime call or launch failed */
+#define UPLIFT_LA_ERR_NO_DEVICE  6  /* no usable sm_100 device              */
+
+/* largest neighbourhood and padding the kernels accept */
+#define UPLIFT_LA_MAX_K  25
+#define UPLIFT_LA_MAX_PN 4
+
+/*
+ * Fused Local Attender forward: 1x1 logit projection (+ residual), softmax
+ * over the K neighbour offsets and softmax-weighted gather-sum of the value
+ * vectors, in one kernel launch on `stream` (a cudaStream_t; NULL = legacy
+ * default stream).
+ *
+ * Replaces LocalAttender.forward (uplift/uplift.py:801-847) and the fast-path
+ * pair _TritonAttenderWrapper.forward (uplift/fast.py:60-64) +
+ * TritonLocalAttender.forward (uplift/kernels/triton_attender.py:335-392).
+ *
+ *   guide   [B, Cg, I*H, I*W]  strides guide_strides (elements)
+ *   value   [B, C,  H,   W  ]  strides value_strides
+ *   weight  [K, Cg] fp32, row-major (conv1.weight[:, :, 0, 0])
+ *   bias    [K] fp32, or NULL for no bias (conv1.bias)
+ *   out     [B, C,  I*H, I*W]  strides out_strides, must not alias inputs
+ *   offsets host array [K][2] of (dy, dx), |dy|,|dx| <= pn
+ *           (LocalAttender.offsets, uplift/uplift.py:746-760)
+ *   K       1..UPLIFT_LA_MAX_K; the reference uses 5, 9, 13, 17, 25
+ *   I       integer scale factor >= 1
+ */
+int uplift_la_forward(const void* guide, const int64_t guide_strides[4],
+                      const void* value, const int64_t value_strides[4],
+                      const float* weight, const float* bias,
+                      void* out, const int64_t out_strides[4],
+                      int B, int Cg, int C, int H, int W, int I, int K,
+                      const int8_t* offsets, int pn, int conv_res,
+                      int dtype, int hardmax, void* stream);
+
+/*
+ * Softmax-pool from pre-projected logits: the same kernel with the
+ * projection replaced by a read of `logits` [B, K, I*H, I*W] (any strides,
+ * same storage type as value).  Replaces the Triton fused kernels'
+ * interface TritonLocalAttender.forward(att, x, hardmax)
+ * (uplift/kernels/triton_attender.py:336) and its PyTorch fallback
+ * (uplift/kernels/triton_attender.py:402-431), for every K and I instead of
+ * K=17, I in {2,4} only.
+ */
+int uplift_la_pool(const void* logits, const int64_t logits_strides[4],
+                   const void* value, const int64_t value_strides[4],
+                   void* out, const int64_t out_strides[4],
+                   int B, int C, int H, int W, int I, int K,
+                   const int8_t* offsets, int pn,
+                   int dtype, int hardmax, void* stream);
+
+/* Message for the last non-OK status returned on the calling thread. */
+const char* uplift_la_last_error(void);
+
+/* Name of a status code. */
+const char* uplift_la_status_string(int status);
+
+/* ABI version: (major << 16) | minor. */
+int uplift_la_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UPLIFT_LA_H_ */

@@ -1,0 +1,93 @@
+"""ctypes binding of the C ABI in include/uplift_la.h.
+
+This is the only way the package reaches the GPU kernels.  Loading fails
+loudly (RuntimeError) when the library is missing: there is no CPU or
+PyTorch fallback anywhere in the product path.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+from . import build as _build
+
+F32, BF16, F16 = 0, 1, 2
+OK, ERR_ARG, ERR_SHAPE, ERR_LAYOUT, ERR_OFFSETS, ERR_CUDA, ERR_NO_DEVICE = range(7)
+MAX_K = 25
+MAX_PN = 4
+
+# every symbol include/uplift_la.h declares
+EXPORTED = (
+    "uplift_la_forward",
+    "uplift_la_pool",
+    "uplift_la_last_error",
+    "uplift_la_status_string",
+    "uplift_la_abi_version",
+)
+
+_lib = None
+_lock = threading.Lock()
+
+_I64_4 = ctypes.c_int64 * 4
+
+
+def lib_path() -> Path:
+    return _build.lib_path()
+
+
+def load(build_if_missing: bool = False):
+    """Load libuplift_la.so once; raise RuntimeError if it is not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = lib_path()
+        if not path.exists():
+            if build_if_missing:
+                _build.build()
+            else:
+                raise RuntimeError(
+                    f"uplift_b200 CUDA library not found at {path}; build it with "
+                    "`python -m uplift_b200.build` (there is no CPU fallback)")
+        lib = ctypes.CDLL(str(path))
+        vp, i, i64p = ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int64)
+        i8p, fp = ctypes.POINTER(ctypes.c_int8), ctypes.c_void_p
+        lib.uplift_la_forward.restype = i
+        lib.uplift_la_forward.argtypes = [vp, i64p, vp, i64p, fp, fp, vp, i64p,
+                                          i, i, i, i, i, i, i, i8p, i, i, i, i, vp]
+        lib.uplift_la_pool.restype = i
+        lib.uplift_la_pool.argtypes = [vp, i64p, vp, i64p, vp, i64p,
+                                       i, i, i, i, i, i, i8p, i, i, i, vp]
+        lib.uplift_la_last_error.restype = ctypes.c_char_p
+        lib.uplift_la_last_error.argtypes = []
+        lib.uplift_la_status_string.restype = ctypes.c_char_p
+        lib.uplift_la_status_string.argtypes = [i]
+        lib.uplift_la_abi_version.restype = i
+        lib.uplift_la_abi_version.argtypes = []
+        _lib = lib
+    return _lib
+
+
+def strides(t) -> "ctypes.Array":
+    return _I64_4(*[int(s) for s in t.stride()])
+
+
+def offsets_array(offsets):
+    flat = [int(v) for off in offsets for v in off]
+    return (ctypes.c_int8 * len(flat))(*flat)
+
+
+def check(rc: int, what: str) -> None:
+    """Turn a status code into a Python exception."""
+    if rc == OK:
+        return
+    lib = load()
+    msg = lib.uplift_la_last_error().decode(errors="replace")
+    name = lib.uplift_la_status_string(rc).decode()
+    text = f"{what}: {name} ({rc}): {msg}"
+    if rc in (ERR_ARG, ERR_SHAPE, ERR_LAYOUT, ERR_OFFSETS):
+        raise ValueError(text)
+    raise RuntimeError(text)

@@ -1,0 +1,602 @@
+// Fused UPLiFT Local Attender forward for B200 (sm_100a).
+//
+// One launch computes, for every output pixel of a tile, the 1x1 logit
+// projection of the guide (residual folded into the weights), the softmax
+// over the K neighbour offsets and the softmax-weighted gather-sum of the
+// C-channel value vectors of the parent cell's neighbours.  Reference
+// semantics: LocalAttender.forward, uplift/uplift.py:801-847 (projection
+// :810-812, replicate-padded neighbour gather :784-798 / :823, softmax over
+// K :828, child mapping [B,D,H,I,W,I] :829-830, pooling :835-846).
+//
+// Work decomposition
+//   unit  = CPT output pixels ("children") of one coarse cell that share the
+//           K neighbour value vectors (CPT = 4: the 2x2 children of a cell
+//           for I = 2, or one row of 4 children for I = 4; CPT = 1 else).
+//   tile  = kTilePix output pixels = kTilePix / CPT units, processed by one
+//           CTA in two phases:
+//     A. logits: two threads per pixel split the guide channels, reduce with
+//        one shuffle, add bias, softmax (fp32) -> shared memory.  The
+//        per-unit neighbour offsets and output offsets are also staged.
+//     B. pooling: a thread owns (unit, 16-byte channel vector); per offset
+//        k it loads one value vector (coalesced NHWC, read-only path) and
+//        accumulates CPT children with packed fp32 FMA (FFMA2).
+//   The grid is persistent (a multiple of the SM count); the projection
+//   weights are staged in shared memory once per CTA.
+//
+// Storage is NHWC (channel stride 1); accumulation is fp32 throughout.
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdarg.h>
+#include <string.h>
+
+#include <algorithm>
+#include <type_traits>
+
+#include "uplift_la.h"
+
+namespace ula {
+
+constexpr int kThreads = 256;
+constexpr int kTilePix = 128;          // output pixels per tile (2 threads each in phase A)
+constexpr int kMaxK = UPLIFT_LA_MAX_K;
+
+struct Params {
+  const void* guide;  int64_t g_b, g_h, g_w;
+  const void* logits; int64_t l_b, l_k, l_h, l_w;
+  const void* value;  int64_t v_b, v_h, v_w;
+  void* out;          int64_t o_b, o_h, o_w;
+  const float* weight;
+  const float* bias;
+  int B, Cg, C, H, W, I;
+  int conv_res, hardmax, from_logits, guide_vec;
+  int units_per_cell;    // I*I / CPT
+  int num_units;         // B*H*W*units_per_cell
+  int num_tiles;
+  int8_t dy[kMaxK];
+  int8_t dx[kMaxK];
+};
+
+// ---------------------------------------------------------------- storage types
+template <typename T> struct Elem;
+
+template <> struct Elem<float> {
+  static constexpr int kVec = 4;  // elements per 16-byte vector
+  __device__ __forceinline__ static float to_f(float x) { return x; }
+  __device__ __forceinline__ static void unpack(const uint4& u, float* f) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]),
+                      __float_as_uint(f[2]), __float_as_uint(f[3]));
+  }
+  __device__ __forceinline__ static float from_f(float x) { return x; }
+};
+
+template <> struct Elem<__nv_bfloat16> {
+  static constexpr int kVec = 8;
+  __device__ __forceinline__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  // bf16 -> fp32 is exact: the bf16 bits are the high half of the fp32 bits.
+  __device__ __forceinline__ static void unpack_word(uint32_t w, float& lo, float& hi) {
+    lo = __uint_as_float(w << 16);
+    hi = __uint_as_float(w & 0xffff0000u);
+  }
+  __device__ __forceinline__ static void unpack(const uint4& u, float* f) {
+    unpack_word(u.x, f[0], f[1]); unpack_word(u.y, f[2], f[3]);
+    unpack_word(u.z, f[4], f[5]); unpack_word(u.w, f[6], f[7]);
+  }
+  __device__ __forceinline__ static uint32_t pack_word(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(pack_word(f[0], f[1]), pack_word(f[2], f[3]),
+                      pack_word(f[4], f[5]), pack_word(f[6], f[7]));
+  }
+  __device__ __forceinline__ static __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+};
+
+template <> struct Elem<__half> {
+  static constexpr int kVec = 8;
+  __device__ __forceinline__ static float to_f(__half x) { return __half2float(x); }
+  __device__ __forceinline__ static void unpack_word(uint32_t w, float& lo, float& hi) {
+    __half2 h = *reinterpret_cast<__half2*>(&w);
+    float2 f = __half22float2(h);
+    lo = f.x; hi = f.y;
+  }
+  __device__ __forceinline__ static void unpack(const uint4& u, float* f) {
+    unpack_word(u.x, f[0], f[1]); unpack_word(u.y, f[2], f[3]);
+    unpack_word(u.z, f[4], f[5]); unpack_word(u.w, f[6], f[7]);
+  }
+  __device__ __forceinline__ static uint32_t pack_word(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(pack_word(f[0], f[1]), pack_word(f[2], f[3]),
+                      pack_word(f[4], f[5]), pack_word(f[6], f[7]));
+  }
+  __device__ __forceinline__ static __half from_f(float x) { return __float2half_rn(x); }
+};
+
+__device__ __forceinline__ uint4 ldg_nc16(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+__device__ __forceinline__ int clampi(int v, int lo, int hi) { return min(max(v, lo), hi); }
+
+// Shared-memory layout (floats / ints), sized on the host by smem_bytes().
+template <int K, int CPT>
+struct Smem {
+  static constexpr int kKP = (K + 3) & ~3;        // padded logit count
+  static constexpr int kUnits = kTilePix / CPT;
+  // offsets in 4-byte words
+  static constexpr int kP = 0;                               // [units][K][CPT] fp32 weights
+  static constexpr int kNbr = kP + kUnits * K * CPT;         // [units][K] int32 value offsets
+  static constexpr int kOut = (kNbr + kUnits * K + 1) & ~1;  // [units][CPT] int64 out offsets
+  static constexpr int kBias = kOut + 2 * kUnits * CPT;      // [kKP]
+  static constexpr int kW = (kBias + kKP + 3) & ~3;          // [Cg][kKP] (projection only)
+  static size_t bytes(int Cg, bool from_logits) {
+    return 4 * (size_t)(kW + (from_logits ? 0 : Cg * kKP));
+  }
+};
+
+template <typename T, int K, int CPT, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+la_fwd_kernel(const __grid_constant__ Params p) {
+  using E = Elem<T>;
+  using S = Smem<K, CPT>;
+  constexpr int KP = S::kKP;
+  constexpr int NU = S::kUnits;
+  constexpr int V = VEC ? E::kVec : 1;
+
+  extern __shared__ __align__(16) float smem[];
+  float* s_p = smem + S::kP;
+  int* s_nbr = reinterpret_cast<int*>(smem + S::kNbr);
+  long long* s_out = reinterpret_cast<long long*>(smem + S::kOut);
+  float* s_bias = smem + S::kBias;
+  float* s_w = smem + S::kW;
+
+  const int tid = threadIdx.x;
+
+  // Stage the projection once per CTA.  The residual guide[:, :K] of
+  // residual_auto (uplift/uplift.py:26-39) is linear in the guide, so it is
+  // folded into the weights: logit = (W + E) g + b with E[k][c] = (k == c).
+  if (!p.from_logits) {
+    for (int i = tid; i < p.Cg * KP; i += kThreads) {
+      const int c = i / KP, k = i - c * KP;
+      float w = 0.f;
+      if (k < K) {
+        w = p.weight[(size_t)k * p.Cg + c];
+        if (p.conv_res && k == c) w += 1.f;
+      }
+      s_w[i] = w;
+    }
+    for (int k = tid; k < KP; k += kThreads)
+      s_bias[k] = (p.bias != nullptr && k < K) ? p.bias[k] : 0.f;
+  }
+
+  const T* __restrict__ gbase = static_cast<const T*>(p.guide);
+  const T* __restrict__ lbase = static_cast<const T*>(p.logits);
+  const T* __restrict__ vbase = static_cast<const T*>(p.value);
+  T* __restrict__ obase = static_cast<T*>(p.out);
+
+  for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    __syncthreads();  // previous tile's phase B is done with shared memory
+
+    // ------------------------------------------------------------ phase A
+    {
+      const int pix = tid >> 1, half = tid & 1;
+      const int u = pix / CPT, t = pix - u * CPT;
+      const int unit = tile * NU + u;
+      const bool valid = unit < p.num_units;
+
+      int b = 0, cy = 0, cx = 0, y = 0, x = 0;
+      if (valid) {
+        const int sub = unit % p.units_per_cell;
+        const int cell = unit / p.units_per_cell;
+        cx = cell % p.W;
+        const int rest = cell / p.W;
+        cy = rest % p.H;
+        b = rest / p.H;
+        const int ch = sub * CPT + t;
+        const int ci = ch / p.I;
+        y = cy * p.I + ci;
+        x = cx * p.I + (ch - ci * p.I);
+      }
+
+      float logit[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) logit[k] = 0.f;
+
+      if (p.from_logits) {
+        if (valid && half == 0) {
+          const T* lp = lbase + b * p.l_b + y * p.l_h + x * p.l_w;
+#pragma unroll
+          for (int k = 0; k < K; ++k) logit[k] = E::to_f(lp[k * p.l_k]);
+        }
+      } else {
+        if (valid) {
+          const T* gp = gbase + b * p.g_b + y * p.g_h + x * p.g_w;
+          if (p.guide_vec) {
+            for (int c0 = half * E::kVec; c0 < p.Cg; c0 += 2 * E::kVec) {
+              float g[E::kVec];
+              E::unpack(ldg_nc16(gp + c0), g);
+#pragma unroll
+              for (int e = 0; e < E::kVec; ++e) {
+                const float* wr = s_w + (c0 + e) * KP;
+#pragma unroll
+                for (int k4 = 0; k4 < KP; k4 += 4) {
+                  const float4 w4 = *reinterpret_cast<const float4*>(wr + k4);
+                  if (k4 + 0 < K) logit[k4 + 0] = fmaf(w4.x, g[e], logit[k4 + 0]);
+                  if (k4 + 1 < K) logit[k4 + 1] = fmaf(w4.y, g[e], logit[k4 + 1]);
+                  if (k4 + 2 < K) logit[k4 + 2] = fmaf(w4.z, g[e], logit[k4 + 2]);
+                  if (k4 + 3 < K) logit[k4 + 3] = fmaf(w4.w, g[e], logit[k4 + 3]);
+                }
+              }
+            }
+          } else {
+            for (int c = half; c < p.Cg; c += 2) {
+              const float g = E::to_f(gp[c]);
+              const float* wr = s_w + c * KP;
+#pragma unroll
+              for (int k = 0; k < K; ++k) logit[k] = fmaf(wr[k], g, logit[k]);
+            }
+          }
+        }
+        // combine the two channel halves (all lanes participate)
+#pragma unroll
+        for (int k = 0; k < K; ++k) logit[k] += __shfl_xor_sync(0xffffffffu, logit[k], 1);
+#pragma unroll
+        for (int k = 0; k < K; ++k) logit[k] += s_bias[k];
+      }
+
+      if (half == 0) {
+        float* pw = s_p + u * K * CPT + t;
+        if (!valid) {
+#pragma unroll
+          for (int k = 0; k < K; ++k) pw[k * CPT] = 0.f;
+        } else if (p.hardmax) {
+          // one-hot of the first maximal logit (torch argmax tie rule)
+          int best = 0;
+          float bv = logit[0];
+#pragma unroll
+          for (int k = 1; k < K; ++k)
+            if (logit[k] > bv) { bv = logit[k]; best = k; }
+#pragma unroll
+          for (int k = 0; k < K; ++k) pw[k * CPT] = (k == best) ? 1.f : 0.f;
+        } else {
+          float m = logit[0];
+#pragma unroll
+          for (int k = 1; k < K; ++k) m = fmaxf(m, logit[k]);
+          float s = 0.f;
+#pragma unroll
+          for (int k = 0; k < K; ++k) { logit[k] = __expf(logit[k] - m); s += logit[k]; }
+          const float inv = 1.f / s;
+#pragma unroll
+          for (int k = 0; k < K; ++k) pw[k * CPT] = logit[k] * inv;
+        }
+        // per-unit neighbour offsets (replicate padding == clamping) and
+        // per-child output offsets
+        if (valid) {
+          if (t == 0) {
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+              const int ny = clampi(cy + p.dy[k], 0, p.H - 1);
+              const int nx = clampi(cx + p.dx[k], 0, p.W - 1);
+              s_nbr[u * K + k] = (int)(ny * p.v_h + nx * p.v_w);
+            }
+          }
+          s_out[u * CPT + t] = b * p.o_b + y * p.o_h + x * p.o_w;
+        }
+      }
+    }
+    __syncthreads();
+
+    // ------------------------------------------------------------ phase B
+    {
+      const int NG = p.C / V;
+      const int tile_units = min(NU, p.num_units - tile * NU);
+      const int items = tile_units * NG;
+      for (int it = tid; it < items; it += kThreads) {
+        const int u = it / NG;
+        const int gi = it - u * NG;
+        const int unit = tile * NU + u;
+        const int b = (unit / p.units_per_cell) / (p.H * p.W);
+        const T* vb = vbase + b * p.v_b + gi * V;
+        const int* nb = s_nbr + u * K;
+        const float* pw = s_p + u * K * CPT;
+
+        if constexpr (V >= 2) {
+          float2 acc[CPT][V / 2];
+#pragma unroll
+          for (int t = 0; t < CPT; ++t)
+#pragma unroll
+            for (int e = 0; e < V / 2; ++e) acc[t][e] = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+            float v[V];
+            E::unpack(ldg_nc16(vb + nb[k]), v);
+            float pk[CPT];
+            if constexpr (CPT == 4) {
+              const float4 q = *reinterpret_cast<const float4*>(pw + k * CPT);
+              pk[0] = q.x; pk[1] = q.y; pk[2] = q.z; pk[3] = q.w;
+            } else {
+#pragma unroll
+              for (int t = 0; t < CPT; ++t) pk[t] = pw[k * CPT + t];
+            }
+#pragma unroll
+            for (int t = 0; t < CPT; ++t) {
+              const float2 pp = make_float2(pk[t], pk[t]);
+#pragma unroll
+              for (int e = 0; e < V / 2; ++e)
+                acc[t][e] = __ffma2_rn(make_float2(v[2 * e], v[2 * e + 1]), pp, acc[t][e]);
+            }
+          }
+#pragma unroll
+          for (int t = 0; t < CPT; ++t) {
+            float o[V];
+#pragma unroll
+            for (int e = 0; e < V / 2; ++e) { o[2 * e] = acc[t][e].x; o[2 * e + 1] = acc[t][e].y; }
+            T* op = obase + s_out[u * CPT + t] + gi * V;
+            *reinterpret_cast<uint4*>(op) = E::pack(o);
+          }
+        } else {
+          float acc[CPT];
+#pragma unroll
+          for (int t = 0; t < CPT; ++t) acc[t] = 0.f;
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+            const float v = E::to_f(vb[nb[k]]);
+#pragma unroll
+            for (int t = 0; t < CPT; ++t) acc[t] = fmaf(pw[k * CPT + t], v, acc[t]);
+          }
+#pragma unroll
+          for (int t = 0; t < CPT; ++t) obase[s_out[u * CPT + t] + gi] = E::from_f(acc[t]);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- host side
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+using KernelFn = void (*)(Params);
+
+template <typename T, int K, int CPT>
+KernelFn pick_vec(bool vec) {
+  return vec ? la_fwd_kernel<T, K, CPT, true> : la_fwd_kernel<T, K, CPT, false>;
+}
+
+template <typename T, int K>
+KernelFn pick_cpt(int cpt, bool vec) {
+  return cpt == 4 ? pick_vec<T, K, 4>(vec) : pick_vec<T, K, 1>(vec);
+}
+
+template <typename T>
+KernelFn pick_k(int K, int cpt, bool vec) {
+  switch (K) {
+    case 5: return pick_cpt<T, 5>(cpt, vec);
+    case 9: return pick_cpt<T, 9>(cpt, vec);
+    case 13: return pick_cpt<T, 13>(cpt, vec);
+    case 17: return pick_cpt<T, 17>(cpt, vec);
+    case 25: return pick_cpt<T, 25>(cpt, vec);
+    default: return nullptr;
+  }
+}
+
+size_t smem_for(int K, int cpt, int Cg, bool from_logits) {
+  auto f = [&](auto kk, auto cc) { return Smem<decltype(kk)::value, decltype(cc)::value>::bytes(Cg, from_logits); };
+  using I1 = std::integral_constant<int, 1>;
+  using I4 = std::integral_constant<int, 4>;
+#define ULA_SM(KV)                                                          \
+  case KV:                                                                  \
+    return cpt == 4 ? f(std::integral_constant<int, KV>{}, I4{})            \
+                    : f(std::integral_constant<int, KV>{}, I1{});
+  switch (K) {
+    ULA_SM(5) ULA_SM(9) ULA_SM(13) ULA_SM(17) ULA_SM(25)
+    default: return 0;
+  }
+#undef ULA_SM
+}
+
+size_t elem_size(int dtype) { return dtype == UPLIFT_LA_F32 ? 4 : 2; }
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+struct DevInfo {
+  int sms = 0;
+  size_t max_smem_optin = 0;
+};
+
+int device_info(DevInfo* info) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_NO_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
+  static DevInfo cache[64];
+  if (dev < 64 && cache[dev].sms > 0) { *info = cache[dev]; return UPLIFT_LA_OK; }
+  int sms = 0, major = 0, optin = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+  if (major != 10) return fail(UPLIFT_LA_ERR_NO_DEVICE, "device %d has compute capability %d.x; this build targets sm_100a", dev, major);
+  info->sms = sms;
+  info->max_smem_optin = (size_t)optin;
+  if (dev < 64) cache[dev] = *info;
+  return UPLIFT_LA_OK;
+}
+
+int launch(const Params& p0, int dtype, int K, int cpt, bool vec, size_t smem, cudaStream_t stream) {
+  Params p = p0;
+  if (p.num_units == 0) return UPLIFT_LA_OK;  // empty input: nothing to do
+  KernelFn fn = nullptr;
+  switch (dtype) {
+    case UPLIFT_LA_F32: fn = pick_k<float>(K, cpt, vec); break;
+    case UPLIFT_LA_BF16: fn = pick_k<__nv_bfloat16>(K, cpt, vec); break;
+    case UPLIFT_LA_F16: fn = pick_k<__half>(K, cpt, vec); break;
+    default: return fail(UPLIFT_LA_ERR_ARG, "unknown dtype %d", dtype);
+  }
+  if (fn == nullptr) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d unsupported (5, 9, 13, 17, 25)", K);
+
+  DevInfo info;
+  int rc = device_info(&info);
+  if (rc != UPLIFT_LA_OK) return rc;
+  if (smem > info.max_smem_optin)
+    return fail(UPLIFT_LA_ERR_SHAPE, "guide channels Cg=%d need %zu B of shared memory (max %zu)", p.Cg, smem, info.max_smem_optin);
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem);
+  if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "occupancy query: %s", cudaGetErrorString(e));
+  if (per_sm < 1) per_sm = 1;
+  const int grid = (int)std::min<int64_t>((int64_t)p.num_tiles, (int64_t)info.sms * per_sm);
+  fn<<<grid, kThreads, smem, stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return UPLIFT_LA_OK;
+}
+
+int check_common(const void* value, const int64_t* vs, void* out, const int64_t* os,
+                 int B, int C, int H, int W, int I, int K, const int8_t* offsets, int pn, int dtype,
+                 Params* p, int* cpt, bool* vec) {
+  if (dtype != UPLIFT_LA_F32 && dtype != UPLIFT_LA_BF16 && dtype != UPLIFT_LA_F16)
+    return fail(UPLIFT_LA_ERR_ARG, "unknown dtype %d", dtype);
+  if (vs == nullptr || os == nullptr || offsets == nullptr)
+    return fail(UPLIFT_LA_ERR_ARG, "null stride or offset array");
+  if (B < 0 || C < 1 || H < 0 || W < 0 || I < 1)
+    return fail(UPLIFT_LA_ERR_SHAPE, "bad sizes B=%d C=%d H=%d W=%d I=%d", B, C, H, W, I);
+  if (K < 1 || K > kMaxK) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d out of range", K);
+  if (pn < 0 || pn > UPLIFT_LA_MAX_PN) return fail(UPLIFT_LA_ERR_OFFSETS, "pn=%d out of range", pn);
+  for (int k = 0; k < K; ++k) {
+    const int dy = offsets[2 * k], dx = offsets[2 * k + 1];
+    if (dy < -pn || dy > pn || dx < -pn || dx > pn)
+      return fail(UPLIFT_LA_ERR_OFFSETS, "offset %d = (%d, %d) exceeds pn=%d", k, dy, dx, pn);
+    p->dy[k] = (int8_t)dy;
+    p->dx[k] = (int8_t)dx;
+  }
+  if (vs[1] != 1 || os[1] != 1)
+    return fail(UPLIFT_LA_ERR_LAYOUT, "value and out need channel stride 1 (channels_last), got %lld / %lld",
+                (long long)vs[1], (long long)os[1]);
+  const int64_t units64 = (int64_t)B * H * W;
+  int upc;
+  if (I == 1) { *cpt = 1; upc = 1; }
+  else if (I == 2) { *cpt = 4; upc = 1; }
+  else if (I == 4) { *cpt = 4; upc = 4; }
+  else { *cpt = 1; upc = I * I; }
+  if (units64 * upc >= ((int64_t)1 << 31))
+    return fail(UPLIFT_LA_ERR_SHAPE, "too many cells (%lld)", (long long)(units64 * upc));
+  if ((int64_t)(H > 0 ? H - 1 : 0) * vs[2] + (int64_t)(W > 0 ? W - 1 : 0) * vs[3] + C >= ((int64_t)1 << 31))
+    return fail(UPLIFT_LA_ERR_SHAPE, "one value image exceeds 2^31 elements");
+  if (B > 0 && H > 0 && W > 0) {
+    if (value == nullptr || out == nullptr) return fail(UPLIFT_LA_ERR_ARG, "null value/out pointer");
+  }
+  const size_t es = elem_size(dtype);
+  const int vec_elems = 16 / (int)es;
+  *vec = (C % vec_elems == 0) && aligned16(value) && aligned16(out) &&
+         (vs[0] % vec_elems == 0) && (vs[2] % vec_elems == 0) && (vs[3] % vec_elems == 0) &&
+         (os[0] % vec_elems == 0) && (os[2] % vec_elems == 0) && (os[3] % vec_elems == 0);
+  p->value = value; p->v_b = vs[0]; p->v_h = vs[2]; p->v_w = vs[3];
+  p->out = out; p->o_b = os[0]; p->o_h = os[2]; p->o_w = os[3];
+  p->B = B; p->C = C; p->H = H; p->W = W; p->I = I;
+  p->units_per_cell = upc;
+  p->num_units = (int)(units64 * upc);
+  const int nu = kTilePix / *cpt;
+  p->num_tiles = (p->num_units + nu - 1) / nu;
+  return UPLIFT_LA_OK;
+}
+
+}  // namespace ula
+
+extern "C" {
+
+int uplift_la_forward(const void* guide, const int64_t guide_strides[4],
+                      const void* value, const int64_t value_strides[4],
+                      const float* weight, const float* bias,
+                      void* out, const int64_t out_strides[4],
+                      int B, int Cg, int C, int H, int W, int I, int K,
+                      const int8_t* offsets, int pn, int conv_res,
+                      int dtype, int hardmax, void* stream) {
+  using namespace ula;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  int cpt = 1;
+  bool vec = false;
+  int rc = check_common(value, value_strides, out, out_strides, B, C, H, W, I, K, offsets, pn, dtype, &p, &cpt, &vec);
+  if (rc != UPLIFT_LA_OK) return rc;
+  if (guide_strides == nullptr) return fail(UPLIFT_LA_ERR_ARG, "null guide strides");
+  if (Cg < 1) return fail(UPLIFT_LA_ERR_SHAPE, "Cg=%d", Cg);
+  if (guide_strides[1] != 1)
+    return fail(UPLIFT_LA_ERR_LAYOUT, "guide needs channel stride 1 (channels_last), got %lld", (long long)guide_strides[1]);
+  if (p.num_units > 0 && (guide == nullptr || weight == nullptr))
+    return fail(UPLIFT_LA_ERR_ARG, "null guide/weight pointer");
+  const int gv = 16 / (int)elem_size(dtype);
+  p.guide = guide;
+  p.g_b = guide_strides[0]; p.g_h = guide_strides[2]; p.g_w = guide_strides[3];
+  p.guide_vec = (Cg % gv == 0) && aligned16(guide) && p.g_b % gv == 0 && p.g_h % gv == 0 && p.g_w % gv == 0;
+  p.weight = weight;
+  p.bias = bias;
+  p.Cg = Cg;
+  p.conv_res = conv_res ? 1 : 0;
+  p.hardmax = hardmax ? 1 : 0;
+  p.from_logits = 0;
+  const size_t smem = smem_for(K, cpt, Cg, false);
+  if (smem == 0) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d unsupported (5, 9, 13, 17, 25)", K);
+  return launch(p, dtype, K, cpt, vec, smem, static_cast<cudaStream_t>(stream));
+}
+
+int uplift_la_pool(const void* logits, const int64_t logits_strides[4],
+                   const void* value, const int64_t value_strides[4],
+                   void* out, const int64_t out_strides[4],
+                   int B, int C, int H, int W, int I, int K,
+                   const int8_t* offsets, int pn,
+                   int dtype, int hardmax, void* stream) {
+  using namespace ula;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  int cpt = 1;
+  bool vec = false;
+  int rc = check_common(value, value_strides, out, out_strides, B, C, H, W, I, K, offsets, pn, dtype, &p, &cpt, &vec);
+  if (rc != UPLIFT_LA_OK) return rc;
+  if (logits_strides == nullptr) return fail(UPLIFT_LA_ERR_ARG, "null logits strides");
+  if (p.num_units > 0 && logits == nullptr) return fail(UPLIFT_LA_ERR_ARG, "null logits pointer");
+  p.logits = logits;
+  p.l_b = logits_strides[0]; p.l_k = logits_strides[1]; p.l_h = logits_strides[2]; p.l_w = logits_strides[3];
+  p.hardmax = hardmax ? 1 : 0;
+  p.from_logits = 1;
+  const size_t smem = smem_for(K, cpt, 0, true);
+  if (smem == 0) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d unsupported (5, 9, 13, 17, 25)", K);
+  return launch(p, dtype, K, cpt, vec, smem, static_cast<cudaStream_t>(stream));
+}
+
+const char* uplift_la_last_error(void) { return ula::g_err; }
+
+const char* uplift_la_status_string(int status) {
+  switch (status) {
+    case UPLIFT_LA_OK: return "ok";
+    case UPLIFT_LA_ERR_ARG: return "invalid argument";
+    case UPLIFT_LA_ERR_SHAPE: return "unsupported or inconsistent shape";
+    case UPLIFT_LA_ERR_LAYOUT: return "unsupported layout";
+    case UPLIFT_LA_ERR_OFFSETS: return "bad neighbour offsets";
+    case UPLIFT_LA_ERR_CUDA: return "CUDA error";
+    case UPLIFT_LA_ERR_NO_DEVICE: return "no usable sm_100 device";
+    default: return "unknown status";
+  }
+}
+
+int uplift_la_abi_version(void) { return (1 << 16) | 0; }
+
+}  // extern "C"

@@ -1,0 +1,176 @@
+"""Torch-facing Local Attender operators over the C ABI.
+
+`local_attender` (guide -> logits -> softmax -> pooled values) and
+`attender_pool` (pre-projected logits -> pooled values) launch the sm_100a
+kernels of libuplift_la.so on the current CUDA stream.  Both are also
+registered as torch custom ops (``torch.ops.uplift_b200.*``) with fake
+implementations, so torch.compile traces them without a graph break (the
+reference's Triton module takes one, uplift/kernels/triton_attender.py:335).
+
+Inputs are accepted in any layout; the kernels read channels_last (NHWC)
+storage, so other layouts are converted first.  The output is channels_last
+in the value dtype.
+"""
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import torch
+
+from . import _native
+
+_DTYPES = {torch.float32: _native.F32, torch.bfloat16: _native.BF16, torch.float16: _native.F16}
+
+
+def _nhwc(t: torch.Tensor) -> torch.Tensor:
+    if t.stride(1) == 1 and t.is_contiguous(memory_format=torch.channels_last):
+        return t
+    if t.stride(1) == 1:  # sliced / padded channels_last view: strides are passed through
+        return t
+    return t.contiguous(memory_format=torch.channels_last)
+
+
+def _check_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError(
+                "uplift_b200 Local Attender runs on CUDA (sm_100) tensors only; got a "
+                f"{t.device} tensor (there is no CPU fallback)")
+        if t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} vs {t.device}")
+    return dev
+
+
+def _offsets_flat(offsets) -> list[int]:
+    return [int(v) for off in offsets for v in off]
+
+
+def _scale(Ho: int, Wo: int, H: int, W: int) -> int:
+    if H == 0 or W == 0:
+        raise ValueError("value map has an empty spatial dimension")
+    I = Ho // H
+    if I < 1 or I * H != Ho or I * W != Wo:
+        raise ValueError(f"output size {Ho}x{Wo} is not an integer multiple of the value size {H}x{W}")
+    return I
+
+
+def local_attender_raw(guide: torch.Tensor, value: torch.Tensor, weight: torch.Tensor,
+                       bias: Optional[torch.Tensor], offsets: Sequence, pn: int,
+                       conv_res: bool = True, hardmax: bool = False,
+                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Launch uplift_la_forward.  weight: fp32 [K, Cg] (other dtypes/shapes
+    are converted), bias: fp32 [K] or None."""
+    dev = _check_cuda(guide, value, weight)
+    if guide.dtype != value.dtype:
+        raise ValueError(f"guide dtype {guide.dtype} != value dtype {value.dtype}")
+    if value.dtype not in _DTYPES:
+        raise ValueError(f"unsupported dtype {value.dtype} (float32, bfloat16, float16)")
+    if guide.dim() != 4 or value.dim() != 4:
+        raise ValueError("guide and value must be 4-D [B, C, H, W]")
+    B, C, H, W = value.shape
+    Bg, Cg, Ho, Wo = guide.shape
+    if Bg != B:
+        raise ValueError(f"batch mismatch: guide {Bg} vs value {B}")
+    I = _scale(Ho, Wo, H, W)
+    K = len(offsets)
+    w = weight.detach().reshape(K, -1)
+    if w.shape[1] != Cg:
+        raise ValueError(f"weight has {w.shape[1]} input channels, guide has {Cg}")
+    if w.dtype != torch.float32 or not w.is_contiguous():
+        w = w.to(torch.float32).contiguous()
+    b = None
+    if bias is not None:
+        b = bias.detach()
+        if b.dtype != torch.float32 or not b.is_contiguous():
+            b = b.to(torch.float32).contiguous()
+    g = _nhwc(guide)
+    v = _nhwc(value)
+    if out is None:
+        out = torch.empty((B, C, Ho, Wo), dtype=value.dtype, device=dev,
+                          memory_format=torch.channels_last)
+    lib = _native.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        rc = lib.uplift_la_forward(
+            g.data_ptr(), _native.strides(g), v.data_ptr(), _native.strides(v),
+            w.data_ptr(), None if b is None else b.data_ptr(),
+            out.data_ptr(), _native.strides(out),
+            B, Cg, C, H, W, I, K, _native.offsets_array(offsets), int(pn), int(bool(conv_res)),
+            _DTYPES[value.dtype], int(bool(hardmax)), stream)
+    _native.check(rc, "uplift_la_forward")
+    return out
+
+
+def attender_pool_raw(logits: torch.Tensor, value: torch.Tensor, offsets: Sequence, pn: int,
+                      hardmax: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Launch uplift_la_pool on pre-projected logits [B, K, I*H, I*W]."""
+    dev = _check_cuda(logits, value)
+    if logits.dtype != value.dtype:
+        logits = logits.to(value.dtype)
+    if value.dtype not in _DTYPES:
+        raise ValueError(f"unsupported dtype {value.dtype} (float32, bfloat16, float16)")
+    B, C, H, W = value.shape
+    Bl, K, Ho, Wo = logits.shape
+    if Bl != B:
+        raise ValueError(f"batch mismatch: logits {Bl} vs value {B}")
+    if K != len(offsets):
+        raise ValueError(f"logits have {K} channels but {len(offsets)} offsets were given")
+    I = _scale(Ho, Wo, H, W)
+    v = _nhwc(value)
+    if out is None:
+        out = torch.empty((B, C, Ho, Wo), dtype=value.dtype, device=dev,
+                          memory_format=torch.channels_last)
+    lib = _native.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        rc = lib.uplift_la_pool(
+            logits.data_ptr(), _native.strides(logits), v.data_ptr(), _native.strides(v),
+            out.data_ptr(), _native.strides(out), B, C, H, W, I, K,
+            _native.offsets_array(offsets), int(pn), _DTYPES[value.dtype], int(bool(hardmax)), stream)
+    _native.check(rc, "uplift_la_pool")
+    return out
+
+
+# ----------------------------------------------------------------- custom ops
+def _pairs(flat: Sequence[int]):
+    return [(flat[i], flat[i + 1]) for i in range(0, len(flat), 2)]
+
+
+@torch.library.custom_op("uplift_b200::local_attender", mutates_args=())
+def _local_attender_op(guide: torch.Tensor, value: torch.Tensor, weight: torch.Tensor,
+                       bias: Optional[torch.Tensor], offsets: list[int], pn: int,
+                       conv_res: bool, hardmax: bool) -> torch.Tensor:
+    return local_attender_raw(guide, value, weight, bias, _pairs(offsets), pn, conv_res, hardmax)
+
+
+@_local_attender_op.register_fake
+def _(guide, value, weight, bias, offsets, pn, conv_res, hardmax):
+    B, C = value.shape[0], value.shape[1]
+    return value.new_empty((B, C, guide.shape[2], guide.shape[3])).contiguous(
+        memory_format=torch.channels_last)
+
+
+@torch.library.custom_op("uplift_b200::attender_pool", mutates_args=())
+def _attender_pool_op(logits: torch.Tensor, value: torch.Tensor, offsets: list[int], pn: int,
+                      hardmax: bool) -> torch.Tensor:
+    return attender_pool_raw(logits, value, _pairs(offsets), pn, hardmax)
+
+
+@_attender_pool_op.register_fake
+def _(logits, value, offsets, pn, hardmax):
+    B, C = value.shape[0], value.shape[1]
+    return value.new_empty((B, C, logits.shape[2], logits.shape[3])).contiguous(
+        memory_format=torch.channels_last)
+
+
+def local_attender(guide, value, weight, bias, offsets, pn, conv_res=True, hardmax=False):
+    """Fused Local Attender (custom op entry; traceable by torch.compile)."""
+    return torch.ops.uplift_b200.local_attender(guide, value, weight, bias, _offsets_flat(offsets),
+                                                int(pn), bool(conv_res), bool(hardmax))
+
+
+def attender_pool(logits, value, offsets, pn, hardmax=False):
+    """Softmax-pool from pre-projected logits (custom op entry)."""
+    return torch.ops.uplift_b200.attender_pool(logits, value, _offsets_flat(offsets), int(pn),
+                                               bool(hardmax))
