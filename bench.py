@@ -51,7 +51,8 @@ def algo_bytes_per_pixel(Cg=CG, Cv=C, I=2, s=ELEM):
     return Cg * s + Cv * s + Cv * s / (I * I)
 
 
-def out_pixels(B=B_PER_GPU):
+def out_pixels(B=None):
+    B = B_PER_GPU if B is None else B
     return sum(B * fo * fo for _, fo in LEVELS)
 
 
@@ -154,9 +155,10 @@ def max_over_ranks(x: float, world: int, dev) -> float:
     return float(t.item())
 
 
-def make_inputs(dev, B=B_PER_GPU, seed=0):
+def make_inputs(dev, B=None, seed=0):
     """Guides for the four levels and the level-0 value map (bf16, NHWC)."""
     from uplift_b200.attender import LocalAttender
+    B = B_PER_GPU if B is None else B
     g = torch.Generator().manual_seed(seed)
     torch.manual_seed(seed)
     la = LocalAttender(CG, K_NBR).to(torch.bfloat16)  # default nn.Conv2d init under seed 0

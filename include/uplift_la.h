@@ -96,6 +96,29 @@ int uplift_la_pool(const void* logits, const int64_t logits_strides[4],
                    const int8_t* offsets, int pn,
                    int dtype, int hardmax, void* stream);
 
+/* Kernel selection for uplift_la_forward (process-wide; default AUTO).
+ * AUTO picks the tensor-core kernel (tcgen05 MMA, TMEM accumulators, TMA)
+ * when it applies -- bf16/fp16 storage, I = 2, Cg = 64, C a multiple of 64
+ * up to 384, 16-byte aligned tensors -- and the CUDA-core kernel otherwise;
+ * SIMT always uses the CUDA-core kernel; TENSOR_CORE makes ineligible
+ * problems fail with UPLIFT_LA_ERR_SHAPE instead of falling back.  No
+ * reference counterpart (the reference has a single Triton kernel family). */
+#define UPLIFT_LA_POLICY_AUTO        0
+#define UPLIFT_LA_POLICY_SIMT        1
+#define UPLIFT_LA_POLICY_TENSOR_CORE 2
+int uplift_la_set_kernel_policy(int policy);
+
+/* Kernel launched by the last successful call on the calling thread. */
+#define UPLIFT_LA_KERNEL_SIMT        1
+#define UPLIFT_LA_KERNEL_TENSOR_CORE 2
+int uplift_la_last_kernel(void);
+
+/* Device status word of the tensor-core kernel: 0 when every launch so far
+ * completed its pipeline, else the role (1 producer, 2 MMA, 3 softmax,
+ * 4 epilogue) whose bounded wait expired first.  Synchronises with the
+ * device; `clear` resets the word.  Returns -1 if the read failed. */
+int uplift_la_device_status(int clear);
+
 /* Message for the last non-OK status returned on the calling thread. */
 const char* uplift_la_last_error(void);
 

@@ -24,7 +24,12 @@ EXPORTED = (
     "uplift_la_last_error",
     "uplift_la_status_string",
     "uplift_la_abi_version",
+    "uplift_la_set_kernel_policy",
+    "uplift_la_last_kernel",
+    "uplift_la_device_status",
 )
+POLICY_AUTO, POLICY_SIMT, POLICY_TENSOR_CORE = 0, 1, 2
+KERNEL_SIMT, KERNEL_TENSOR_CORE = 1, 2
 
 _lib = None
 _lock = threading.Lock()
@@ -67,6 +72,12 @@ def load(build_if_missing: bool = False):
         lib.uplift_la_status_string.argtypes = [i]
         lib.uplift_la_abi_version.restype = i
         lib.uplift_la_abi_version.argtypes = []
+        lib.uplift_la_set_kernel_policy.restype = i
+        lib.uplift_la_set_kernel_policy.argtypes = [i]
+        lib.uplift_la_last_kernel.restype = i
+        lib.uplift_la_last_kernel.argtypes = []
+        lib.uplift_la_device_status.restype = i
+        lib.uplift_la_device_status.argtypes = [i]
         _lib = lib
     return _lib
 
@@ -91,3 +102,27 @@ def check(rc: int, what: str) -> None:
     if rc in (ERR_ARG, ERR_SHAPE, ERR_LAYOUT, ERR_OFFSETS):
         raise ValueError(text)
     raise RuntimeError(text)
+
+
+class kernel_policy:
+    """Context manager selecting the kernel family (AUTO / SIMT / TENSOR_CORE)."""
+
+    def __init__(self, policy: int):
+        self.policy = policy
+
+    def __enter__(self):
+        check(load().uplift_la_set_kernel_policy(self.policy), "uplift_la_set_kernel_policy")
+        return self
+
+    def __exit__(self, *exc):
+        load().uplift_la_set_kernel_policy(POLICY_AUTO)
+        return False
+
+
+def last_kernel() -> int:
+    return load().uplift_la_last_kernel()
+
+
+def device_status(clear: bool = True) -> int:
+    """0 if every tensor-core launch completed its pipeline (synchronises)."""
+    return load().uplift_la_device_status(int(clear))

@@ -1,0 +1,36 @@
+// Internal interface between the C-ABI front end (local_attender.cu) and
+// the tensor-core kernel (la_tc.cu).  Not part of the public ABI.
+#pragma once
+
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+namespace ula {
+
+// Everything the tensor-core path needs; strides in elements, channel
+// stride 1 (NHWC).
+struct TcArgs {
+  const void* guide; int64_t g_b, g_h, g_w;
+  const void* value; int64_t v_b, v_h, v_w;
+  void* out;         int64_t o_b, o_h, o_w;
+  const float* weight;  // [K, Cg] fp32, device
+  const float* bias;    // [K] fp32 or null
+  int B, Cg, C, H, W, K, pn;
+  int conv_res, hardmax, dtype;
+  const int8_t* offsets;  // host [K][2]
+};
+
+// True when the tensor-core kernel supports the problem (sizes, alignment).
+bool tc_eligible(const TcArgs& a, const char** why);
+
+// Launch the tensor-core kernel; returns a UPLIFT_LA_* status.
+int tc_launch(const TcArgs& a, cudaStream_t stream);
+
+// Read (and optionally clear) the tensor-core kernel's device status word;
+// -1 if the read failed.
+int tc_device_status(bool clear);
+
+// Record an error message for uplift_la_last_error().
+int fail(int code, const char* fmt, ...);
+
+}  // namespace ula

@@ -1,0 +1,687 @@
+// Tensor-core Local Attender for B200 (sm_100a): tcgen05 MMA with TMEM
+// accumulators, TMA tile loads/stores, mbarrier pipelines, warp-specialised.
+//
+// For the bf16 / fp16 path with scale I = 2 (every shipped UPLiFT config),
+// Cg = 64 guide channels and C a multiple of 64 (<= 384) value channels.
+//
+// Formulation.  A tile is 4 x 8 coarse cells = 8 x 16 output pixels
+// (M = 128).  All K neighbours of all its cells lie in an 8 x 12 window of
+// coarse pixels (pn <= 2), so for the tile
+//
+//     logits[128 x 32]  = G[128 x 64] . W^T[64 x 32]          (MMA 1)
+//     A[128 x 96]       = softmax weights scattered to window columns
+//     out[128 x C]      = A[128 x 96] . Vwin[96 x C]           (MMA 2)
+//
+// MMA 2 is a banded GEMM (17 of 96 entries per row are non-zero); on the
+// 5th-gen tensor cores the wasted products are cheaper than the FP32 FMA
+// pipe doing only the useful ones, so the kernel stays HBM-bound.  The
+// softmax weights are rounded to the storage type (bf16 / fp16) as in the
+// reference's low-precision path (F.softmax on a bf16 tensor); every sum
+// is accumulated in fp32 in TMEM.  Replicate padding: window pixels outside
+// the image are zero-filled by TMA and never referenced, because each
+// offset is clamped to the image before being mapped to a window column
+// (clamped duplicates are merged in fp32 first).
+//
+// Roles (320 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer: guide tile, value window in 64-channel chunks
+//   warp 1      TMEM owner + single-thread MMA issuer
+//   warps 2-5   logits -> (+bias, +residual) -> softmax -> A matrix
+//   warps 6-9   TMEM -> registers -> storage type -> smem -> TMA store
+// Every mbarrier wait is bounded (2 s); on expiry the CTA records an error
+// code in a device status word, drains its outstanding async work and exits.
+//
+// Reference semantics: LocalAttender.forward, uplift/uplift.py:801-847.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+
+#include "uplift_la.h"
+#include "la_internal.h"
+
+namespace ula {
+
+// Status word for in-kernel failures (bounded waits that expired); read and
+// cleared through uplift_la_device_status().
+__device__ unsigned int g_tc_status;
+
+namespace tc {
+
+constexpr int kCellsY = 4, kCellsX = 8;      // cells per tile
+constexpr int kM = 128;                      // output pixels per tile (8 x 16)
+constexpr int kWinX = 12, kWin = 96;         // value window 8 x 12 (pn <= 2)
+constexpr int kKSteps = kWin / 16;           // MMA-2 K steps
+constexpr int kChunk = 64;                   // channels per value / output chunk
+constexpr int kMaxC = 384;
+constexpr int kNV = 8;                       // value-chunk ring slots
+constexpr int kLogN = 32;                    // MMA-1 N (K <= 32 logits)
+constexpr int kLogCol = kMaxC;               // TMEM column of the logit accumulators
+constexpr int kTmemCols = 512;
+constexpr int kThreads = 320;
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+
+constexpr int kVBytes = kWin * 128;          // 12 KB: 96 window px x 64 ch
+constexpr int kGBytes = kM * 128;            // 16 KB: 128 px x 64 guide ch
+constexpr int kStageBytes = kM * 128;        // 16 KB: 128 px x 64 out ch
+constexpr int kWBytes = kLogN * 128;         // 4 KB: 32 logits x 64 ch
+constexpr int kA2Bytes = kM * kWin * 2;      // 24 KB
+constexpr int kA2Sbo = (kWin / 8) * 128;     // 1536 B between 8-row groups of A
+
+constexpr int kOffV = 0;
+constexpr int kOffG = kOffV + kNV * kVBytes;
+constexpr int kOffStage = kOffG + 2 * kGBytes;
+constexpr int kOffW = kOffStage + 2 * kStageBytes;
+constexpr int kOffA2 = kOffW + kWBytes;
+constexpr int kOffBar = kOffA2 + 2 * kA2Bytes;
+constexpr int kNumBars = 2 + 2 + kNV + kNV + 2 + 2 + 2 + 2 + 1 + 1 + 1;
+constexpr int kOffMisc = kOffBar + kNumBars * 8;   // tmem slot, abort flag
+constexpr int kOffBias = kOffMisc + 16;
+constexpr int kSmemBytes = kOffBias + kLogN * 4 + 1024;  // + base alignment slack
+
+struct Params {
+  CUtensorMap gmap;   // guide  [B, 2H, 2W, 64]      box {64, 16, 8, 1}
+  CUtensorMap vmap;   // value  [B, H, W, C]         box {64, 12, 8, 1}
+  CUtensorMap omap;   // out    [B, 2H, 2W, C]       box {64, 16, 8, 1}
+  const float* weight;  // [K][64] fp32
+  const float* bias;    // [K] fp32 or null
+  int8_t dy[kLogN];
+  int8_t dx[kLogN];
+  int H, W, nchunks, tiles_x, tiles_y, num_tiles;
+  int res_k;            // residual channels (min(K, Cg) when conv_res, else 0)
+  int hardmax;
+  int margin;           // max |offset| (cells this close to a border may clamp)
+};
+
+// ------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t su32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of parity `parity` to complete.  Returns false
+// (after flagging the CTA and the device status word) on timeout, or when
+// another role of the CTA has already given up.
+__device__ __noinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, unsigned where) {
+  if (mbar_try(b, parity)) return true;
+  const uint64_t t0 = gtimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try(b, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (gtimer() - t0 > kTimeoutNs) {
+        *abort_flag = 1;
+        atomicCAS(&g_tc_status, 0u, where);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void named_bar(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+      ::"r"(su32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)),
+        "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+      ::"l"(reinterpret_cast<uint64_t>(map)), "r"(su32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 32 lanes x 32 consecutive 32-bit columns: thread (lane) gets its row.
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// Shared-memory matrix descriptors (tcgen05 "matrix descriptor": start
+// address >> 4 in bits 0-13, leading byte offset >> 4 in 16-29, stride
+// byte offset >> 4 in 32-45, version 1 in 46-47, layout type in 61-63).
+__device__ __forceinline__ uint64_t mdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+constexpr uint32_t kLayoutNone = 0, kLayoutSw128 = 2;
+
+// Instruction descriptor, kind::f16: fp32 accumulate, A/B type (0 = f16,
+// 1 = bf16), K-major A, B major per flag, N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_fmt, uint32_t b_mn_major, uint32_t m, uint32_t n) {
+  return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (b_mn_major << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+template <typename T> struct Store;
+template <> struct Store<__nv_bfloat16> {
+  static constexpr uint32_t kFmt = 1;
+  __device__ __forceinline__ static uint16_t bits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+  __device__ __forceinline__ static float from_bits(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+  __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static constexpr CUtensorMapDataType kMapType = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+};
+template <> struct Store<__half> {
+  static constexpr uint32_t kFmt = 0;
+  __device__ __forceinline__ static uint16_t bits(float x) { return __half_as_ushort(__float2half_rn(x)); }
+  __device__ __forceinline__ static float from_bits(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+  __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static constexpr CUtensorMapDataType kMapType = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+};
+
+struct TileXY {
+  int b, cy0, cx0;
+};
+__device__ __forceinline__ TileXY tile_of(const Params& p, int t) {
+  const int per_img = p.tiles_x * p.tiles_y;
+  TileXY r;
+  r.b = t / per_img;
+  const int rem = t - r.b * per_img;
+  const int ty = rem / p.tiles_x;
+  r.cy0 = ty * kCellsY;
+  r.cx0 = (rem - ty * p.tiles_x) * kCellsX;
+  return r;
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constant__ Params p) {
+  using S = Store<T>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sV = smem + kOffV;
+  uint8_t* sG = smem + kOffG;
+  uint8_t* sStage = smem + kOffStage;
+  uint8_t* sW = smem + kOffW;
+  uint8_t* sA2 = smem + kOffA2;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* g_full = bars;
+  uint64_t* g_empty = g_full + 2;
+  uint64_t* v_full = g_empty + 2;
+  uint64_t* v_empty = v_full + kNV;
+  uint64_t* log_full = v_empty + kNV;
+  uint64_t* log_empty = log_full + 2;
+  uint64_t* a2_full = log_empty + 2;
+  uint64_t* a2_empty = a2_full + 2;
+  uint64_t* out_full = a2_empty + 2;
+  uint64_t* out_empty = out_full + 1;
+  uint64_t* drain = out_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
+  float* sBias = reinterpret_cast<float*>(smem + kOffBias);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+
+  // ---------------------------------------------------------------- setup
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&g_full[i], 1);
+      mbar_init(&g_empty[i], 2);  // logits MMA done + residual read done
+      mbar_init(&log_full[i], 1);
+      mbar_init(&log_empty[i], 1);
+      mbar_init(&a2_full[i], 1);
+      mbar_init(&a2_empty[i], 1);
+    }
+    for (int i = 0; i < kNV; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    mbar_init(out_full, 1);
+    mbar_init(out_empty, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // Projection weights in the storage type, K-major with the 128-byte swizzle
+  // (row n = logit n, 64 guide channels per 128-byte row).
+  for (int idx = tid; idx < kLogN * 64; idx += kThreads) {
+    const int n = idx >> 6, c = idx & 63;
+    const float w = (n < K) ? p.weight[n * 64 + c] : 0.f;
+    *reinterpret_cast<uint16_t*>(sW + n * 128 + ((((c >> 3) ^ (n & 7)) << 4)) + (c & 7) * 2) = S::bits(w);
+  }
+  for (int k = tid; k < kLogN; k += kThreads) sBias[k] = (p.bias != nullptr && k < K) ? p.bias[k] : 0.f;
+  fence_proxy_async();  // sW is read by the tensor core (async proxy)
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)), "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  int local_tiles = 0;
+  for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) ++local_tiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_map(&p.gmap);
+      prefetch_map(&p.vmap);
+      prefetch_map(&p.omap);
+      uint32_t vc = 0;
+      bool ok = true;
+      for (int n = 0; n < local_tiles && ok; ++n) {
+        const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+        const int s = n & 1;
+        const uint32_t ph = (n >> 1) & 1;
+        ok = mbar_wait(&g_empty[s], ph ^ 1, abort_flag, 1);
+        if (!ok) break;
+        mbar_expect_tx(&g_full[s], kGBytes);
+        tma_load(sG + s * kGBytes, &p.gmap, &g_full[s], 0, 2 * tl.cx0, 2 * tl.cy0, tl.b);
+        for (int j = 0; j < p.nchunks; ++j, ++vc) {
+          const int slot = vc % kNV;
+          const uint32_t vph = (vc / kNV) & 1;
+          ok = mbar_wait(&v_empty[slot], vph ^ 1, abort_flag, 1);
+          if (!ok) break;
+          mbar_expect_tx(&v_full[slot], kVBytes);
+          tma_load(sV + slot * kVBytes, &p.vmap, &v_full[slot], j * kChunk, tl.cx0 - 2, tl.cy0 - 2, tl.b);
+        }
+      }
+      if (!ok) {  // let issued loads land before the CTA can exit
+        const uint64_t t0 = gtimer();
+        while (gtimer() - t0 < 200000ull) {}
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdLog = idesc_f16(S::kFmt, 0, kM, kLogN);
+      constexpr uint32_t kIdOut = idesc_f16(S::kFmt, 1, kM, kChunk);
+      const uint32_t aW = su32(sW);
+      uint32_t vc = 0;
+      bool ok = true;
+      auto logits = [&](int n) -> bool {
+        const int s = n & 1;
+        const uint32_t ph = (n >> 1) & 1;
+        if (!mbar_wait(&g_full[s], ph, abort_flag, 2)) return false;
+        if (!mbar_wait(&log_empty[s], ph ^ 1, abort_flag, 2)) return false;
+        tc_fence_after();
+        const uint32_t aG = su32(sG + s * kGBytes);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)  // K = 64 guide channels in steps of 16
+          tc_mma(tmem + kLogCol + kLogN * s, mdesc(aG + 32 * k, 16, 1024, kLayoutSw128),
+                 mdesc(aW + 32 * k, 16, 1024, kLayoutSw128), kIdLog, k > 0);
+        tc_commit(&log_full[s]);
+        tc_commit(&g_empty[s]);
+        return true;
+      };
+      if (local_tiles > 0) ok = logits(0);
+      for (int n = 0; n < local_tiles && ok; ++n) {
+        if (n + 1 < local_tiles) {
+          ok = logits(n + 1);
+          if (!ok) break;
+        }
+        const int s = n & 1;
+        const uint32_t ph = (n >> 1) & 1;
+        ok = mbar_wait(&a2_full[s], ph, abort_flag, 2) && mbar_wait(out_empty, (n & 1) ^ 1, abort_flag, 2);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t aA = su32(sA2 + s * kA2Bytes);
+        for (int j = 0; j < p.nchunks; ++j, ++vc) {
+          const int slot = vc % kNV;
+          ok = mbar_wait(&v_full[slot], (vc / kNV) & 1, abort_flag, 2);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t aV = su32(sV + slot * kVBytes);
+#pragma unroll
+          for (int ks = 0; ks < kKSteps; ++ks)
+            tc_mma(tmem + kChunk * j, mdesc(aA + 256 * ks, 128, kA2Sbo, kLayoutNone),
+                   mdesc(aV + 2048 * ks, kVBytes, 1024, kLayoutSw128), kIdOut, ks > 0);
+          tc_commit(&v_empty[slot]);
+        }
+        if (!ok) break;
+        tc_commit(&a2_empty[s]);
+        tc_commit(out_full);
+      }
+      // all issued MMAs complete before TMEM can be released
+      tc_commit(drain);
+      mbar_wait(drain, 0, abort_flag, 2);
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ softmax
+    const int q = warp & 3;
+    const int i = 32 * q + lane;  // TMEM lane == pixel of the tile
+    const int py = i >> 4, px = i & 15;
+    const int cr = py >> 1, cc = px >> 1;
+    const bool leader = (warp == 2 && lane == 0);
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+    for (int n = 0; n < local_tiles; ++n) {
+      const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+      const int s = n & 1;
+      const uint32_t ph = (n >> 1) & 1;
+      if (!mbar_wait(&log_full[s], ph, abort_flag, 3)) break;
+      tc_fence_after();
+      uint32_t r[32];
+      tc_ld32(lane_base + kLogCol + kLogN * s, r);
+      tc_wait_ld();
+      tc_fence_before();
+      named_bar(1, 128);
+      if (leader) mbar_arrive(&log_empty[s]);
+      if (!mbar_wait(&g_full[s], ph, abort_flag, 3)) break;
+
+      float lg[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) lg[k] = __uint_as_float(r[k]) + sBias[k];
+      if (p.res_k > 0) {  // residual_auto: + guide[k] for k < min(K, Cg)
+        const uint8_t* grow = sG + s * kGBytes + i * 128;
+#pragma unroll
+        for (int c8 = 0; c8 < (K + 7) / 8; ++c8) {
+          const uint4 v = *reinterpret_cast<const uint4*>(grow + ((c8 ^ (i & 7)) << 4));
+          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int k = c8 * 8 + e;
+            if (k < K && k < p.res_k)
+              lg[k] += S::from_bits((uint16_t)(w4[e >> 1] >> ((e & 1) * 16)));
+          }
+        }
+      }
+      named_bar(1, 128);
+      if (leader) mbar_arrive(&g_empty[s]);
+
+      float pk[K];
+      if (p.hardmax) {
+        int best = 0;
+        float bv = lg[0];
+#pragma unroll
+        for (int k = 1; k < K; ++k)
+          if (lg[k] > bv) { bv = lg[k]; best = k; }
+#pragma unroll
+        for (int k = 0; k < K; ++k) pk[k] = (k == best) ? 1.f : 0.f;
+      } else {
+        float m = lg[0];
+#pragma unroll
+        for (int k = 1; k < K; ++k) m = fmaxf(m, lg[k]);
+        float z = 0.f;
+#pragma unroll
+        for (int k = 0; k < K; ++k) { pk[k] = __expf(lg[k] - m); z += pk[k]; }
+        const float inv = 1.f / z;
+#pragma unroll
+        for (int k = 0; k < K; ++k) pk[k] *= inv;
+      }
+      // window column of every offset after replicate clamping
+      const int cy = tl.cy0 + cr, cx = tl.cx0 + cc;
+      int idx[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int ny = min(max(cy + p.dy[k], 0), p.H - 1) - (tl.cy0 - 2);
+        const int nx = min(max(cx + p.dx[k], 0), p.W - 1) - (tl.cx0 - 2);
+        idx[k] = ny * kWinX + nx;
+      }
+      uint32_t dup = 0;
+      const bool border = cy < p.margin || cx < p.margin || cy > p.H - 1 - p.margin || cx > p.W - 1 - p.margin;
+      if (border) {  // merge offsets that clamp onto the same pixel
+#pragma unroll
+        for (int k = 1; k < K; ++k) {
+#pragma unroll
+          for (int j = 0; j < k; ++j) {
+            if (!((dup >> k) & 1u) && !((dup >> j) & 1u) && idx[j] == idx[k]) {
+              pk[j] += pk[k];
+              dup |= 1u << k;
+            }
+          }
+        }
+      }
+      if (!mbar_wait(&a2_empty[s], ph ^ 1, abort_flag, 3)) break;
+      // row i of A (K-major, no swizzle: 8x16-byte core matrices; 8-row
+      // groups kA2Sbo apart, 8-column groups 128 B apart)
+      uint8_t* arow = sA2 + s * kA2Bytes + (i >> 3) * kA2Sbo + (i & 7) * 16;
+#pragma unroll
+      for (int j = 0; j < kWin / 8; ++j) *reinterpret_cast<uint4*>(arow + j * 128) = make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int k = 0; k < K; ++k)
+        if (!((dup >> k) & 1u))
+          *reinterpret_cast<uint16_t*>(arow + (idx[k] >> 3) * 128 + (idx[k] & 7) * 2) = S::bits(pk[k]);
+      fence_proxy_async();
+      named_bar(1, 128);
+      if (leader) mbar_arrive(&a2_full[s]);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int i = 32 * q + lane;
+    const bool leader = (warp == 6 && lane == 0);
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+    uint32_t jg = 0;
+    for (int n = 0; n < local_tiles; ++n) {
+      const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+      if (!mbar_wait(out_full, n & 1, abort_flag, 4)) break;
+      tc_fence_after();
+      for (int j = 0; j < p.nchunks; ++j, ++jg) {
+        uint32_t r0[32], r1[32];
+        tc_ld32(lane_base + kChunk * j, r0);
+        tc_ld32(lane_base + kChunk * j + 32, r1);
+        tc_wait_ld();
+        if (j == p.nchunks - 1) tc_fence_before();
+        const int sb = jg & 1;
+        if (leader) bulk_wait_read1();  // the store that last used buffer sb has read it
+        named_bar(2, 128);
+        uint8_t* row = sStage + sb * kStageBytes + i * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t* src = (c < 4) ? (r0 + 8 * c) : (r1 + 8 * (c - 4));
+          uint4 w;
+          w.x = S::pack(__uint_as_float(src[0]), __uint_as_float(src[1]));
+          w.y = S::pack(__uint_as_float(src[2]), __uint_as_float(src[3]));
+          w.z = S::pack(__uint_as_float(src[4]), __uint_as_float(src[5]));
+          w.w = S::pack(__uint_as_float(src[6]), __uint_as_float(src[7]));
+          *reinterpret_cast<uint4*>(row + ((c ^ (i & 7)) << 4)) = w;
+        }
+        fence_proxy_async();
+        named_bar(2, 128);
+        if (leader) {
+          tma_store(&p.omap, sStage + sb * kStageBytes, j * kChunk, 2 * tl.cx0, 2 * tl.cy0, tl.b);
+          bulk_commit();
+        }
+      }
+      if (leader) mbar_arrive(out_empty);
+    }
+    if (leader) bulk_wait_all();
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// ---------------------------------------------------------------- host side
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(ptr);
+  }
+  return fn;
+}
+
+// NHWC 4-D map: dims {C, W, H, B}, element strides in elements.
+int make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int C, int W, int H, int B,
+             int64_t s_w, int64_t s_h, int64_t s_b, int box_c, int box_w, int box_h) {
+  EncodeTiled enc = encode_fn();
+  if (enc == nullptr) return fail(UPLIFT_LA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)s_w * 2, (cuuint64_t)s_h * 2, (cuuint64_t)s_b * 2};
+  const cuuint32_t box[4] = {(cuuint32_t)box_c, (cuuint32_t)box_w, (cuuint32_t)box_h, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(UPLIFT_LA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return UPLIFT_LA_OK;
+}
+
+template <typename T, int K>
+int launch_t(const Params& p, int grid, cudaStream_t stream) {
+  auto fn = la_tc_kernel<T, K>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  fn<<<grid, kThreads, kSmemBytes, stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "tensor-core kernel launch: %s", cudaGetErrorString(e));
+  return UPLIFT_LA_OK;
+}
+
+template <typename T>
+int launch_k(const Params& p, int K, int grid, cudaStream_t stream) {
+  switch (K) {
+    case 5: return launch_t<T, 5>(p, grid, stream);
+    case 9: return launch_t<T, 9>(p, grid, stream);
+    case 13: return launch_t<T, 13>(p, grid, stream);
+    case 17: return launch_t<T, 17>(p, grid, stream);
+    case 25: return launch_t<T, 25>(p, grid, stream);
+    default: return fail(UPLIFT_LA_ERR_SHAPE, "K=%d unsupported", K);
+  }
+}
+
+}  // namespace tc
+
+int tc_device_status(bool clear) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_status, sizeof(v));
+  if (e != cudaSuccess) {
+    fail(UPLIFT_LA_ERR_CUDA, "status read: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  if (clear && v != 0) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_tc_status, &zero, sizeof(zero));
+    if (e != cudaSuccess) {
+      fail(UPLIFT_LA_ERR_CUDA, "status clear: %s", cudaGetErrorString(e));
+      return -1;
+    }
+  }
+  return (int)v;
+}
+
+static bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool tc_eligible(const TcArgs& a, const char** why) {
+  auto no = [&](const char* m) { if (why) *why = m; return false; };
+  if (a.dtype != UPLIFT_LA_BF16 && a.dtype != UPLIFT_LA_F16) return no("storage type is not bf16/fp16");
+  if (a.Cg != 64) return no("guide channels != 64");
+  if (a.C % tc::kChunk != 0 || a.C > tc::kMaxC) return no("value channels not a multiple of 64 up to 384");
+  if (a.K != 5 && a.K != 9 && a.K != 13 && a.K != 17 && a.K != 25) return no("K not in {5, 9, 13, 17, 25}");
+  if (a.pn > 2) return no("pn > 2");
+  if (a.B < 1 || a.H < 1 || a.W < 1) return no("empty problem");
+  if (a.B > 65535 || a.H > (1 << 20) || a.W > (1 << 20)) return no("too large for the tile grid");
+  if (!a16(a.guide) || !a16(a.value) || !a16(a.out)) return no("base pointers not 16-byte aligned");
+  const int64_t st[9] = {a.g_b, a.g_h, a.g_w, a.v_b, a.v_h, a.v_w, a.o_b, a.o_h, a.o_w};
+  for (int i = 0; i < 9; ++i)
+    if (st[i] % 8 != 0 || st[i] <= 0) return no("strides not multiples of 16 bytes");
+  return true;
+}
+
+int tc_launch(const TcArgs& a, cudaStream_t stream) {
+  using namespace tc;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  const CUtensorMapDataType dt = a.dtype == UPLIFT_LA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  int rc = make_map(&p.gmap, dt, a.guide, a.Cg, 2 * a.W, 2 * a.H, a.B, a.g_w, a.g_h, a.g_b, 64, 16, 8);
+  if (rc == UPLIFT_LA_OK) rc = make_map(&p.vmap, dt, a.value, a.C, a.W, a.H, a.B, a.v_w, a.v_h, a.v_b, 64, kWinX, 8);
+  if (rc == UPLIFT_LA_OK) rc = make_map(&p.omap, dt, a.out, a.C, 2 * a.W, 2 * a.H, a.B, a.o_w, a.o_h, a.o_b, 64, 16, 8);
+  if (rc != UPLIFT_LA_OK) return rc;
+  p.weight = a.weight;
+  p.bias = a.bias;
+  int margin = 0;
+  for (int k = 0; k < a.K; ++k) {
+    p.dy[k] = a.offsets[2 * k];
+    p.dx[k] = a.offsets[2 * k + 1];
+    margin = std::max(margin, std::max(abs((int)p.dy[k]), abs((int)p.dx[k])));
+  }
+  p.H = a.H;
+  p.W = a.W;
+  p.nchunks = a.C / kChunk;
+  p.tiles_x = (a.W + kCellsX - 1) / kCellsX;
+  p.tiles_y = (a.H + kCellsY - 1) / kCellsY;
+  const int64_t nt = (int64_t)p.tiles_x * p.tiles_y * a.B;
+  if (nt >= (1ll << 31)) return fail(UPLIFT_LA_ERR_SHAPE, "too many tiles");
+  p.num_tiles = (int)nt;
+  p.res_k = a.conv_res ? std::min(a.K, a.Cg) : 0;
+  p.hardmax = a.hardmax;
+  p.margin = margin;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = (int)std::min<int64_t>(nt, std::max(sms, 1));
+  return a.dtype == UPLIFT_LA_BF16 ? launch_k<__nv_bfloat16>(p, a.K, grid, stream)
+                                   : launch_k<__half>(p, a.K, grid, stream);
+}
+
+}  // namespace ula

@@ -37,6 +37,7 @@
 #include <type_traits>
 
 #include "uplift_la.h"
+#include "la_internal.h"
 
 namespace ula {
 
@@ -365,6 +366,8 @@ la_fwd_kernel(const __grid_constant__ Params p) {
 
 // ---------------------------------------------------------------- host side
 thread_local char g_err[512] = "";
+thread_local int g_last_kernel = 0;
+int g_policy = UPLIFT_LA_POLICY_AUTO;
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -470,13 +473,26 @@ int launch(const Params& p0, int dtype, int K, int cpt, bool vec, size_t smem, c
   return UPLIFT_LA_OK;
 }
 
-int check_common(const void* value, const int64_t* vs, void* out, const int64_t* os,
+// Strides of size-1 dimensions are arbitrary in torch (a [1, C, 1, 1]
+// tensor may report any); replace them with the dense value so alignment
+// checks and tensor maps see a canonical NHWC layout.  s = {b, c, h, w}.
+void canon_strides(int64_t* s, int C, int H, int W, int B) {
+  if (W == 1) s[3] = C;
+  if (H == 1) s[2] = s[3] * W;
+  if (B == 1) s[0] = s[2] * H;
+}
+
+int check_common(const void* value, const int64_t* vs_in, void* out, const int64_t* os_in,
                  int B, int C, int H, int W, int I, int K, const int8_t* offsets, int pn, int dtype,
                  Params* p, int* cpt, bool* vec) {
   if (dtype != UPLIFT_LA_F32 && dtype != UPLIFT_LA_BF16 && dtype != UPLIFT_LA_F16)
     return fail(UPLIFT_LA_ERR_ARG, "unknown dtype %d", dtype);
-  if (vs == nullptr || os == nullptr || offsets == nullptr)
+  if (vs_in == nullptr || os_in == nullptr || offsets == nullptr)
     return fail(UPLIFT_LA_ERR_ARG, "null stride or offset array");
+  int64_t vs[4] = {vs_in[0], vs_in[1], vs_in[2], vs_in[3]};
+  int64_t os[4] = {os_in[0], os_in[1], os_in[2], os_in[3]};
+  canon_strides(vs, C, H, W, B);
+  canon_strides(os, C, I * H, I * W, B);
   if (B < 0 || C < 1 || H < 0 || W < 0 || I < 1)
     return fail(UPLIFT_LA_ERR_SHAPE, "bad sizes B=%d C=%d H=%d W=%d I=%d", B, C, H, W, I);
   if (K < 1 || K > kMaxK) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d out of range", K);
@@ -544,8 +560,10 @@ int uplift_la_forward(const void* guide, const int64_t guide_strides[4],
   if (p.num_units > 0 && (guide == nullptr || weight == nullptr))
     return fail(UPLIFT_LA_ERR_ARG, "null guide/weight pointer");
   const int gv = 16 / (int)elem_size(dtype);
+  int64_t gs[4] = {guide_strides[0], guide_strides[1], guide_strides[2], guide_strides[3]};
+  canon_strides(gs, Cg, I * H, I * W, B);
   p.guide = guide;
-  p.g_b = guide_strides[0]; p.g_h = guide_strides[2]; p.g_w = guide_strides[3];
+  p.g_b = gs[0]; p.g_h = gs[2]; p.g_w = gs[3];
   p.guide_vec = (Cg % gv == 0) && aligned16(guide) && p.g_b % gv == 0 && p.g_h % gv == 0 && p.g_w % gv == 0;
   p.weight = weight;
   p.bias = bias;
@@ -553,9 +571,33 @@ int uplift_la_forward(const void* guide, const int64_t guide_strides[4],
   p.conv_res = conv_res ? 1 : 0;
   p.hardmax = hardmax ? 1 : 0;
   p.from_logits = 0;
+  if (p.num_units == 0) return UPLIFT_LA_OK;
+
+  const int policy = __atomic_load_n(&g_policy, __ATOMIC_RELAXED);
+  if (policy != UPLIFT_LA_POLICY_SIMT && I == 2) {
+    TcArgs a;
+    a.guide = guide; a.g_b = p.g_b; a.g_h = p.g_h; a.g_w = p.g_w;
+    a.value = value; a.v_b = p.v_b; a.v_h = p.v_h; a.v_w = p.v_w;
+    a.out = out; a.o_b = p.o_b; a.o_h = p.o_h; a.o_w = p.o_w;
+    a.weight = weight; a.bias = bias;
+    a.B = B; a.Cg = Cg; a.C = C; a.H = H; a.W = W; a.K = K; a.pn = pn;
+    a.conv_res = p.conv_res; a.hardmax = p.hardmax; a.dtype = dtype; a.offsets = offsets;
+    const char* why = nullptr;
+    if (tc_eligible(a, &why)) {
+      rc = tc_launch(a, static_cast<cudaStream_t>(stream));
+      if (rc == UPLIFT_LA_OK) g_last_kernel = UPLIFT_LA_KERNEL_TENSOR_CORE;
+      return rc;
+    }
+    if (policy == UPLIFT_LA_POLICY_TENSOR_CORE)
+      return fail(UPLIFT_LA_ERR_SHAPE, "tensor-core kernel required but not applicable: %s", why);
+  } else if (policy == UPLIFT_LA_POLICY_TENSOR_CORE) {
+    return fail(UPLIFT_LA_ERR_SHAPE, "tensor-core kernel required but not applicable: scale I=%d != 2", I);
+  }
   const size_t smem = smem_for(K, cpt, Cg, false);
   if (smem == 0) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d unsupported (5, 9, 13, 17, 25)", K);
-  return launch(p, dtype, K, cpt, vec, smem, static_cast<cudaStream_t>(stream));
+  rc = launch(p, dtype, K, cpt, vec, smem, static_cast<cudaStream_t>(stream));
+  if (rc == UPLIFT_LA_OK) g_last_kernel = UPLIFT_LA_KERNEL_SIMT;
+  return rc;
 }
 
 int uplift_la_pool(const void* logits, const int64_t logits_strides[4],
@@ -579,8 +621,21 @@ int uplift_la_pool(const void* logits, const int64_t logits_strides[4],
   p.from_logits = 1;
   const size_t smem = smem_for(K, cpt, 0, true);
   if (smem == 0) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d unsupported (5, 9, 13, 17, 25)", K);
-  return launch(p, dtype, K, cpt, vec, smem, static_cast<cudaStream_t>(stream));
+  rc = launch(p, dtype, K, cpt, vec, smem, static_cast<cudaStream_t>(stream));
+  if (rc == UPLIFT_LA_OK && p.num_units > 0) g_last_kernel = UPLIFT_LA_KERNEL_SIMT;
+  return rc;
 }
+
+int uplift_la_set_kernel_policy(int policy) {
+  if (policy != UPLIFT_LA_POLICY_AUTO && policy != UPLIFT_LA_POLICY_SIMT && policy != UPLIFT_LA_POLICY_TENSOR_CORE)
+    return ula::fail(UPLIFT_LA_ERR_ARG, "unknown kernel policy %d", policy);
+  __atomic_store_n(&ula::g_policy, policy, __ATOMIC_RELAXED);
+  return UPLIFT_LA_OK;
+}
+
+int uplift_la_last_kernel(void) { return ula::g_last_kernel; }
+
+int uplift_la_device_status(int clear) { return ula::tc_device_status(clear != 0); }
 
 const char* uplift_la_last_error(void) { return ula::g_err; }
 
@@ -597,6 +652,6 @@ const char* uplift_la_status_string(int status) {
   }
 }
 
-int uplift_la_abi_version(void) { return (1 << 16) | 0; }
+int uplift_la_abi_version(void) { return (1 << 16) | 1; }
 
 }  // extern "C"
