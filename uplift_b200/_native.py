@@ -7,6 +7,7 @@ PyTorch fallback anywhere in the product path.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
@@ -38,7 +39,9 @@ _I64_4 = ctypes.c_int64 * 4
 
 
 def lib_path() -> Path:
-    return _build.lib_path()
+    """The in-tree library, or the file named by UPLIFT_LA_LIBRARY."""
+    override = os.environ.get("UPLIFT_LA_LIBRARY")
+    return Path(override) if override else _build.lib_path()
 
 
 def load(build_if_missing: bool = False):

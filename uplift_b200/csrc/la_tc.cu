@@ -59,7 +59,8 @@ constexpr int kWinX = 12, kWin = 96;         // value window 8 x 12 (pn <= 2)
 constexpr int kKSteps = kWin / 16;           // MMA-2 K steps
 constexpr int kChunk = 64;                   // channels per value / output chunk
 constexpr int kMaxC = 384;
-constexpr int kNV = 8;                       // value-chunk ring slots
+constexpr int kUnitChunks = 3;               // value chunks per ring unit (one accumulator half)
+constexpr int kNU = 3;                       // value ring units
 constexpr int kLogN = 32;                    // MMA-1 N (K <= 32 logits)
 constexpr int kLogCol = kMaxC;               // TMEM column of the logit accumulators
 constexpr int kTmemCols = 512;
@@ -74,12 +75,14 @@ constexpr int kA2Bytes = kM * kWin * 2;      // 24 KB
 constexpr int kA2Sbo = (kWin / 8) * 128;     // 1536 B between 8-row groups of A
 
 constexpr int kOffV = 0;
-constexpr int kOffG = kOffV + kNV * kVBytes;
+constexpr int kUnitBytes = kUnitChunks * kVBytes;  // 36 KB
+constexpr int kOffG = kOffV + kNU * kUnitBytes;
 constexpr int kOffStage = kOffG + 2 * kGBytes;
 constexpr int kOffW = kOffStage + 2 * kStageBytes;
 constexpr int kOffA2 = kOffW + kWBytes;
 constexpr int kOffBar = kOffA2 + 2 * kA2Bytes;
-constexpr int kNumBars = 2 + 2 + kNV + kNV + 2 + 2 + 2 + 2 + 1 + 1 + 1;
+constexpr int kNumBars = 2 + 2 + kNU + kNU + 2 + 2 + 2 + 2 + 2 + 2 + 1;
+constexpr int kWarpStage = 32 * 128;         // 4 KB: one epilogue warp's 32 px x 64 ch
 constexpr int kOffMisc = kOffBar + kNumBars * 8;   // tmem slot, abort flag
 constexpr int kOffBias = kOffMisc + 16;
 constexpr int kSmemBytes = kOffBias + kLogN * 4 + 1024;  // + base alignment slack
@@ -87,7 +90,7 @@ constexpr int kSmemBytes = kOffBias + kLogN * 4 + 1024;  // + base alignment sla
 struct Params {
   CUtensorMap gmap;   // guide  [B, 2H, 2W, 64]      box {64, 16, 8, 1}
   CUtensorMap vmap;   // value  [B, H, W, C]         box {64, 12, 8, 1}
-  CUtensorMap omap;   // out    [B, 2H, 2W, C]       box {64, 16, 8, 1}
+  CUtensorMap omap;   // out    [B, 2H, 2W, C]       box {64, 16, 2, 1} (one warp's rows)
   const float* weight;  // [K][64] fp32
   const float* bias;    // [K] fp32 or null
   int8_t dy[kLogN];
@@ -263,14 +266,14 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
   uint64_t* g_full = bars;
   uint64_t* g_empty = g_full + 2;
   uint64_t* v_full = g_empty + 2;
-  uint64_t* v_empty = v_full + kNV;
-  uint64_t* log_full = v_empty + kNV;
+  uint64_t* v_empty = v_full + kNU;
+  uint64_t* log_full = v_empty + kNU;
   uint64_t* log_empty = log_full + 2;
   uint64_t* a2_full = log_empty + 2;
   uint64_t* a2_empty = a2_full + 2;
-  uint64_t* out_full = a2_empty + 2;
-  uint64_t* out_empty = out_full + 1;
-  uint64_t* drain = out_empty + 1;
+  uint64_t* out_full = a2_empty + 2;   // per accumulator half
+  uint64_t* out_empty = out_full + 2;
+  uint64_t* drain = out_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
   float* sBias = reinterpret_cast<float*>(smem + kOffBias);
@@ -282,18 +285,18 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&g_full[i], 1);
-      mbar_init(&g_empty[i], 2);  // logits MMA done + residual read done
+      mbar_init(&g_empty[i], 1 + 4);  // logits MMA done + 4 softmax warps read the residual
       mbar_init(&log_full[i], 1);
-      mbar_init(&log_empty[i], 1);
-      mbar_init(&a2_full[i], 1);
+      mbar_init(&log_empty[i], 4);    // 4 softmax warps
+      mbar_init(&a2_full[i], 4);      // 4 softmax warps
       mbar_init(&a2_empty[i], 1);
+      mbar_init(&out_full[i], 1);
+      mbar_init(&out_empty[i], 4);    // 4 epilogue warps
     }
-    for (int i = 0; i < kNV; ++i) {
+    for (int i = 0; i < kNU; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    mbar_init(out_full, 1);
-    mbar_init(out_empty, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -318,6 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
 
   int local_tiles = 0;
   for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) ++local_tiles;
+  const int half_chunks = (p.nchunks + 1) / 2;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -335,13 +339,19 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
         if (!ok) break;
         mbar_expect_tx(&g_full[s], kGBytes);
         tma_load(sG + s * kGBytes, &p.gmap, &g_full[s], 0, 2 * tl.cx0, 2 * tl.cy0, tl.b);
-        for (int j = 0; j < p.nchunks; ++j, ++vc) {
-          const int slot = vc % kNV;
-          const uint32_t vph = (vc / kNV) & 1;
-          ok = mbar_wait(&v_empty[slot], vph ^ 1, abort_flag, 1);
+        // value window, one ring unit per accumulator half (<= 3 chunks of
+        // 64 channels, contiguous so that one MMA spans them)
+        for (int h = 0; h < 2 && ok; ++h) {
+          const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
+          if (j0 >= j1) continue;
+          const int slot = vc % kNU;
+          ok = mbar_wait(&v_empty[slot], ((vc / kNU) & 1) ^ 1, abort_flag, 1);
           if (!ok) break;
-          mbar_expect_tx(&v_full[slot], kVBytes);
-          tma_load(sV + slot * kVBytes, &p.vmap, &v_full[slot], j * kChunk, tl.cx0 - 2, tl.cy0 - 2, tl.b);
+          mbar_expect_tx(&v_full[slot], (j1 - j0) * kVBytes);
+          for (int j = j0; j < j1; ++j)
+            tma_load(sV + slot * kUnitBytes + (j - j0) * kVBytes, &p.vmap, &v_full[slot], j * kChunk,
+                     tl.cx0 - 2, tl.cy0 - 2, tl.b);
+          ++vc;
         }
       }
       if (!ok) {  // let issued loads land before the CTA can exit
@@ -353,7 +363,6 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdLog = idesc_f16(S::kFmt, 0, kM, kLogN);
-      constexpr uint32_t kIdOut = idesc_f16(S::kFmt, 1, kM, kChunk);
       const uint32_t aW = su32(sW);
       uint32_t vc = 0;
       bool ok = true;
@@ -380,25 +389,35 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
         }
         const int s = n & 1;
         const uint32_t ph = (n >> 1) & 1;
-        ok = mbar_wait(&a2_full[s], ph, abort_flag, 2) && mbar_wait(out_empty, (n & 1) ^ 1, abort_flag, 2);
+        ok = mbar_wait(&a2_full[s], ph, abort_flag, 2);
         if (!ok) break;
         tc_fence_after();
         const uint32_t aA = su32(sA2 + s * kA2Bytes);
-        for (int j = 0; j < p.nchunks; ++j, ++vc) {
-          const int slot = vc % kNV;
-          ok = mbar_wait(&v_full[slot], (vc / kNV) & 1, abort_flag, 2);
+        // two accumulator halves so that the epilogue of one overlaps the
+        // MMAs of the other
+        for (int h = 0; h < 2 && ok; ++h) {
+          const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
+          if (j0 >= j1) continue;
+          ok = mbar_wait(&out_empty[h], (n & 1) ^ 1, abort_flag, 2);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t aV = su32(sV + slot * kVBytes);
+          const int slot = vc % kNU;
+          ok = mbar_wait(&v_full[slot], (vc / kNU) & 1, abort_flag, 2);
+          if (!ok) break;
+          tc_fence_after();
+          ++vc;
+          const uint32_t aV = su32(sV + slot * kUnitBytes);
+          const uint32_t id_out = idesc_f16(S::kFmt, 1, kM, kChunk * (j1 - j0));
 #pragma unroll
           for (int ks = 0; ks < kKSteps; ++ks)
-            tc_mma(tmem + kChunk * j, mdesc(aA + 256 * ks, 128, kA2Sbo, kLayoutNone),
-                   mdesc(aV + 2048 * ks, kVBytes, 1024, kLayoutSw128), kIdOut, ks > 0);
+            tc_mma(tmem + kChunk * j0, mdesc(aA + 256 * ks, 128, kA2Sbo, kLayoutNone),
+                   mdesc(aV + 2048 * ks, kVBytes, 1024, kLayoutSw128), id_out, ks > 0);
           tc_commit(&v_empty[slot]);
+          if (!ok) break;
+          tc_commit(&out_full[h]);
         }
         if (!ok) break;
         tc_commit(&a2_empty[s]);
-        tc_commit(out_full);
       }
       // all issued MMAs complete before TMEM can be released
       tc_commit(drain);
@@ -410,7 +429,6 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     const int i = 32 * q + lane;  // TMEM lane == pixel of the tile
     const int py = i >> 4, px = i & 15;
     const int cr = py >> 1, cc = px >> 1;
-    const bool leader = (warp == 2 && lane == 0);
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
     for (int n = 0; n < local_tiles; ++n) {
       const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
@@ -422,8 +440,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       tc_ld32(lane_base + kLogCol + kLogN * s, r);
       tc_wait_ld();
       tc_fence_before();
-      named_bar(1, 128);
-      if (leader) mbar_arrive(&log_empty[s]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&log_empty[s]);
       if (!mbar_wait(&g_full[s], ph, abort_flag, 3)) break;
 
       float lg[K];
@@ -443,8 +461,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
           }
         }
       }
-      named_bar(1, 128);
-      if (leader) mbar_arrive(&g_empty[s]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&g_empty[s]);
 
       float pk[K];
       if (p.hardmax) {
@@ -500,50 +518,80 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
         if (!((dup >> k) & 1u))
           *reinterpret_cast<uint16_t*>(arow + (idx[k] >> 3) * 128 + (idx[k] & 7) * 2) = S::bits(pk[k]);
       fence_proxy_async();
-      named_bar(1, 128);
-      if (leader) mbar_arrive(&a2_full[s]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a2_full[s]);
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Each warp owns TMEM lanes 32q..32q+31 = output rows 2q, 2q+1 of the
+    // tile and stores them with its own TMA box, so warps never wait for
+    // each other.  TMEM loads are software-pipelined one chunk ahead.
     const int q = warp & 3;
-    const int i = 32 * q + lane;
-    const bool leader = (warp == 6 && lane == 0);
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-    uint32_t jg = 0;
-    for (int n = 0; n < local_tiles; ++n) {
-      const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
-      if (!mbar_wait(out_full, n & 1, abort_flag, 4)) break;
-      tc_fence_after();
-      for (int j = 0; j < p.nchunks; ++j, ++jg) {
-        uint32_t r0[32], r1[32];
-        tc_ld32(lane_base + kChunk * j, r0);
-        tc_ld32(lane_base + kChunk * j + 32, r1);
-        tc_wait_ld();
-        if (j == p.nchunks - 1) tc_fence_before();
-        const int sb = jg & 1;
-        if (leader) bulk_wait_read1();  // the store that last used buffer sb has read it
-        named_bar(2, 128);
-        uint8_t* row = sStage + sb * kStageBytes + i * 128;
+    uint8_t* wstage = sStage + q * 2 * kWarpStage;
+    uint32_t jw = 0;
+    uint32_t ra[64], rb[64];
+    bool ok = true;
+    auto tmem_ld64 = [&](uint32_t* r, int j) {
+      tc_ld32(lane_base + kChunk * j, r);
+      tc_ld32(lane_base + kChunk * j + 32, r + 32);
+    };
+    auto emit = [&](const uint32_t* r, int j, const TileXY& tl) {
+      uint8_t* buf = wstage + (jw & 1) * kWarpStage;
+      if (lane == 0) bulk_wait_read1();  // the store that last used `buf` has read it
+      __syncwarp();
+      uint8_t* row = buf + lane * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t* src = (c < 4) ? (r0 + 8 * c) : (r1 + 8 * (c - 4));
-          uint4 w;
-          w.x = S::pack(__uint_as_float(src[0]), __uint_as_float(src[1]));
-          w.y = S::pack(__uint_as_float(src[2]), __uint_as_float(src[3]));
-          w.z = S::pack(__uint_as_float(src[4]), __uint_as_float(src[5]));
-          w.w = S::pack(__uint_as_float(src[6]), __uint_as_float(src[7]));
-          *reinterpret_cast<uint4*>(row + ((c ^ (i & 7)) << 4)) = w;
-        }
-        fence_proxy_async();
-        named_bar(2, 128);
-        if (leader) {
-          tma_store(&p.omap, sStage + sb * kStageBytes, j * kChunk, 2 * tl.cx0, 2 * tl.cy0, tl.b);
-          bulk_commit();
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t* src = r + 8 * c;
+        uint4 w;
+        w.x = S::pack(__uint_as_float(src[0]), __uint_as_float(src[1]));
+        w.y = S::pack(__uint_as_float(src[2]), __uint_as_float(src[3]));
+        w.z = S::pack(__uint_as_float(src[4]), __uint_as_float(src[5]));
+        w.w = S::pack(__uint_as_float(src[6]), __uint_as_float(src[7]));
+        *reinterpret_cast<uint4*>(row + ((c ^ (lane & 7)) << 4)) = w;
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store(&p.omap, buf, j * kChunk, 2 * tl.cx0, 2 * tl.cy0 + 2 * q, tl.b);
+        bulk_commit();
+      }
+      ++jw;
+    };
+    for (int n = 0; n < local_tiles && ok; ++n) {
+      const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+      for (int h = 0; h < 2; ++h) {
+        const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
+        if (j0 >= j1) continue;
+        ok = mbar_wait(&out_full[h], n & 1, abort_flag, 4);
+        if (!ok) break;
+        tc_fence_after();
+        tmem_ld64(ra, j0);
+        for (int j = j0; j < j1; j += 2) {
+          tc_wait_ld();  // ra = chunk j
+          if (j + 1 < j1) {
+            tmem_ld64(rb, j + 1);
+          } else {
+            tc_fence_before();  // last TMEM read of this half is complete
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&out_empty[h]);
+          }
+          emit(ra, j, tl);
+          if (j + 1 >= j1) break;
+          tc_wait_ld();  // rb = chunk j + 1
+          if (j + 2 < j1) {
+            tmem_ld64(ra, j + 2);
+          } else {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&out_empty[h]);
+          }
+          emit(rb, j + 1, tl);
         }
       }
-      if (leader) mbar_arrive(out_empty);
     }
-    if (leader) bulk_wait_all();
+    if (lane == 0) bulk_wait_all();
   }
 
   // ---------------------------------------------------------------- teardown
@@ -655,7 +703,7 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
   const CUtensorMapDataType dt = a.dtype == UPLIFT_LA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   int rc = make_map(&p.gmap, dt, a.guide, a.Cg, 2 * a.W, 2 * a.H, a.B, a.g_w, a.g_h, a.g_b, 64, 16, 8);
   if (rc == UPLIFT_LA_OK) rc = make_map(&p.vmap, dt, a.value, a.C, a.W, a.H, a.B, a.v_w, a.v_h, a.v_b, 64, kWinX, 8);
-  if (rc == UPLIFT_LA_OK) rc = make_map(&p.omap, dt, a.out, a.C, 2 * a.W, 2 * a.H, a.B, a.o_w, a.o_h, a.o_b, 64, 16, 8);
+  if (rc == UPLIFT_LA_OK) rc = make_map(&p.omap, dt, a.out, a.C, 2 * a.W, 2 * a.H, a.B, a.o_w, a.o_h, a.o_b, 64, 16, 2);
   if (rc != UPLIFT_LA_OK) return rc;
   p.weight = a.weight;
   p.bias = a.bias;
