@@ -636,10 +636,16 @@ int make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int C, 
 }
 
 template <typename T, int K>
-int launch_t(const Params& p, int grid, cudaStream_t stream) {
+int launch_t(const Params& p, int dev, int grid, cudaStream_t stream) {
   auto fn = la_tc_kernel<T, K>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  // the shared-memory opt-in is per function and device; set it once
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  cudaError_t e;
   fn<<<grid, kThreads, kSmemBytes, stream>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "tensor-core kernel launch: %s", cudaGetErrorString(e));
@@ -647,13 +653,13 @@ int launch_t(const Params& p, int grid, cudaStream_t stream) {
 }
 
 template <typename T>
-int launch_k(const Params& p, int K, int grid, cudaStream_t stream) {
+int launch_k(const Params& p, int K, int dev, int grid, cudaStream_t stream) {
   switch (K) {
-    case 5: return launch_t<T, 5>(p, grid, stream);
-    case 9: return launch_t<T, 9>(p, grid, stream);
-    case 13: return launch_t<T, 13>(p, grid, stream);
-    case 17: return launch_t<T, 17>(p, grid, stream);
-    case 25: return launch_t<T, 25>(p, grid, stream);
+    case 5: return launch_t<T, 5>(p, dev, grid, stream);
+    case 9: return launch_t<T, 9>(p, dev, grid, stream);
+    case 13: return launch_t<T, 13>(p, dev, grid, stream);
+    case 17: return launch_t<T, 17>(p, dev, grid, stream);
+    case 25: return launch_t<T, 25>(p, dev, grid, stream);
     default: return fail(UPLIFT_LA_ERR_SHAPE, "K=%d unsupported", K);
   }
 }
@@ -724,12 +730,17 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
   p.res_k = a.conv_res ? std::min(a.K, a.Cg) : 0;
   p.hardmax = a.hardmax;
   p.margin = margin;
-  int dev = 0, sms = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(UPLIFT_LA_ERR_NO_DEVICE, "cudaGetDevice failed");
+  static int sm_count[64] = {};
+  int sms = (dev >= 0 && dev < 64) ? sm_count[dev] : 0;
+  if (sms == 0) {
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (dev >= 0 && dev < 64) sm_count[dev] = sms;
+  }
   const int grid = (int)std::min<int64_t>(nt, std::max(sms, 1));
-  return a.dtype == UPLIFT_LA_BF16 ? launch_k<__nv_bfloat16>(p, a.K, grid, stream)
-                                   : launch_k<__half>(p, a.K, grid, stream);
+  return a.dtype == UPLIFT_LA_BF16 ? launch_k<__nv_bfloat16>(p, a.K, dev, grid, stream)
+                                   : launch_k<__half>(p, a.K, dev, grid, stream);
 }
 
 }  // namespace ula
