@@ -64,7 +64,7 @@ constexpr int kNU = 3;                       // value ring units
 constexpr int kLogN = 32;                    // MMA-1 N (K <= 32 logits)
 constexpr int kLogCol = kMaxC;               // TMEM column of the logit accumulators
 constexpr int kTmemCols = 512;
-constexpr int kThreads = 320;
+constexpr int kThreads = 576;                // 18 warps
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 
 constexpr int kVBytes = kWin * 128;          // 12 KB: 96 window px x 64 ch
@@ -168,7 +168,7 @@ __device__ __forceinline__ void tma_store(const CUtensorMap* map, const void* sr
       : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -423,14 +423,17 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       tc_commit(drain);
       mbar_wait(drain, 0, abort_flag, 2);
     }
-  } else if (warp < 6) {
+  } else if (warp < 10) {
     // ------------------------------------------------------------ softmax
+    // two warpgroups: warps 2-5 take the even tiles (slot 0), warps 6-9 the
+    // odd tiles (slot 1); each warp owns TMEM lane quarter warp % 4
     const int q = warp & 3;
+    const int wg = (warp - 2) >> 2;
     const int i = 32 * q + lane;  // TMEM lane == pixel of the tile
     const int py = i >> 4, px = i & 15;
     const int cr = py >> 1, cc = px >> 1;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-    for (int n = 0; n < local_tiles; ++n) {
+    for (int n = wg; n < local_tiles; n += 2) {
       const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
       const int s = n & 1;
       const uint32_t ph = (n >> 1) & 1;
@@ -523,71 +526,47 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Each warp owns TMEM lanes 32q..32q+31 = output rows 2q, 2q+1 of the
-    // tile and stores them with its own TMA box, so warps never wait for
-    // each other.  TMEM loads are software-pipelined one chunk ahead.
+    // two warpgroups, one per accumulator half: warps 10-13 drain half 0,
+    // warps 14-17 half 1.  Each warp owns TMEM lanes 32q..32q+31 = output
+    // rows 2q, 2q+1 of the tile and stores them with its own TMA box from its
+    // own staging buffer, so warps never wait for each other.
     const int q = warp & 3;
+    const int h = (warp - 10) >> 2;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-    uint8_t* wstage = sStage + q * 2 * kWarpStage;
-    uint32_t jw = 0;
-    uint32_t ra[64], rb[64];
-    bool ok = true;
-    auto tmem_ld64 = [&](uint32_t* r, int j) {
-      tc_ld32(lane_base + kChunk * j, r);
-      tc_ld32(lane_base + kChunk * j + 32, r + 32);
-    };
-    auto emit = [&](const uint32_t* r, int j, const TileXY& tl) {
-      uint8_t* buf = wstage + (jw & 1) * kWarpStage;
-      if (lane == 0) bulk_wait_read1();  // the store that last used `buf` has read it
-      __syncwarp();
-      uint8_t* row = buf + lane * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t* src = r + 8 * c;
-        uint4 w;
-        w.x = S::pack(__uint_as_float(src[0]), __uint_as_float(src[1]));
-        w.y = S::pack(__uint_as_float(src[2]), __uint_as_float(src[3]));
-        w.z = S::pack(__uint_as_float(src[4]), __uint_as_float(src[5]));
-        w.w = S::pack(__uint_as_float(src[6]), __uint_as_float(src[7]));
-        *reinterpret_cast<uint4*>(row + ((c ^ (lane & 7)) << 4)) = w;
-      }
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) {
-        tma_store(&p.omap, buf, j * kChunk, 2 * tl.cx0, 2 * tl.cy0 + 2 * q, tl.b);
-        bulk_commit();
-      }
-      ++jw;
-    };
-    for (int n = 0; n < local_tiles && ok; ++n) {
+    uint8_t* buf = sStage + (warp - 10) * kWarpStage;
+    const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
+    for (int n = 0; n < local_tiles && j0 < j1; ++n) {
       const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
-      for (int h = 0; h < 2; ++h) {
-        const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
-        if (j0 >= j1) continue;
-        ok = mbar_wait(&out_full[h], n & 1, abort_flag, 4);
-        if (!ok) break;
-        tc_fence_after();
-        tmem_ld64(ra, j0);
-        for (int j = j0; j < j1; j += 2) {
-          tc_wait_ld();  // ra = chunk j
-          if (j + 1 < j1) {
-            tmem_ld64(rb, j + 1);
-          } else {
-            tc_fence_before();  // last TMEM read of this half is complete
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&out_empty[h]);
-          }
-          emit(ra, j, tl);
-          if (j + 1 >= j1) break;
-          tc_wait_ld();  // rb = chunk j + 1
-          if (j + 2 < j1) {
-            tmem_ld64(ra, j + 2);
-          } else {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&out_empty[h]);
-          }
-          emit(rb, j + 1, tl);
+      if (!mbar_wait(&out_full[h], n & 1, abort_flag, 4)) break;
+      tc_fence_after();
+      for (int j = j0; j < j1; ++j) {
+        uint32_t r[64];
+        tc_ld32(lane_base + kChunk * j, r);
+        tc_ld32(lane_base + kChunk * j + 32, r + 32);
+        tc_wait_ld();
+        if (j + 1 == j1) {  // last TMEM read of this half is complete
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&out_empty[h]);
+        }
+        if (lane == 0) bulk_wait_read0();  // previous store from `buf` has read it
+        __syncwarp();
+        uint8_t* row = buf + lane * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t* src = r + 8 * c;
+          uint4 w;
+          w.x = S::pack(__uint_as_float(src[0]), __uint_as_float(src[1]));
+          w.y = S::pack(__uint_as_float(src[2]), __uint_as_float(src[3]));
+          w.z = S::pack(__uint_as_float(src[4]), __uint_as_float(src[5]));
+          w.w = S::pack(__uint_as_float(src[6]), __uint_as_float(src[7]));
+          *reinterpret_cast<uint4*>(row + ((c ^ (lane & 7)) << 4)) = w;
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store(&p.omap, buf, j * kChunk, 2 * tl.cx0, 2 * tl.cy0 + 2 * q, tl.b);
+          bulk_commit();
         }
       }
     }
