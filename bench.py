@@ -264,6 +264,9 @@ def run_ours(args, world, rank, local):
     # ---- end to end through the public module with pinned host buffers
     e2e = None if args.no_e2e else run_e2e(la, host, dev, stream, world, args, mpix_step)
 
+    # ---- whole upsampler throughput (weak scaling: 8 images per GPU)
+    ups = None if args.no_upsampler else run_upsampler(dev, stream, world, args)
+
     # ---- CPU baseline (rank 0, N=1 only): reference algorithm on host cores
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -292,6 +295,8 @@ def run_ours(args, world, rank, local):
         "gpu_launches": len(LEVELS) * args.steps,
         "clocks": clk,
     }
+    if ups is not None:
+        result["upsampler"] = ups
     if cpu is not None:
         result["cpu_baseline"] = cpu
     return result
@@ -334,6 +339,45 @@ def run_e2e(la, host, dev, stream, world, args, mpix_step):
     return {"value": round(world * mpix_step / (e_ms / 1e3), 2), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms, 3),
             "api": "uplift_b200.LocalAttender.forward, pinned host buffers"}
+
+
+def run_upsampler(dev, stream, world, args, img_px=448, feat_px=32, iters=4, images=8):
+    """Whole-upsampler throughput: the DINOv2-S/14 UPLiFT (random init, bf16,
+    eval) at img_px, iters=4, outsize=img_px, `images` per GPU; encoder and
+    decoder convs in cuDNN, the attender is the fused kernel.  Inputs are
+    resident on the device (synthetic, seed 0)."""
+    from uplift_b200.configs import get_config
+    from uplift_b200.uplift import UPLiFT
+    cfg = get_config("dinov2-s14")
+    torch.manual_seed(0)
+    model = UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift, dtype=torch.bfloat16).eval().to(dev)
+    model = model.to(memory_format=torch.channels_last)
+    model.enable_iterative(iters)
+    g = torch.Generator().manual_seed(0)
+    img = torch.rand(images, 3, img_px, img_px, generator=g).to(torch.bfloat16).to(dev)
+    feats = torch.randn(images, 384, feat_px, feat_px, generator=g).to(torch.bfloat16).to(dev)
+    img = img.contiguous(memory_format=torch.channels_last)
+    feats = feats.contiguous(memory_format=torch.channels_last)
+    steps = max(2, min(args.steps, 10))
+    with torch.inference_mode():
+        for _ in range(max(args.warmup, 2)):
+            model(img, feats, [img_px, img_px])
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            out = model(img, feats, [img_px, img_px])
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
+    assert out.shape == (images, 384, img_px, img_px)
+    return {"img_per_s": round(world * images / (ms / 1e3), 2), "ms_per_batch": round(ms, 3),
+            "images_per_gpu": images, "global_images": images * world, "steps": steps,
+            "config": f"UPLiFT DINOv2-S/14 random-init, bf16, {img_px}px, feats 384x{feat_px}^2, iters={iters}, "
+                      f"outsize={img_px}, channels_last; convs cuDNN (TF32 default), attender fused kernel"}
 
 
 def cpu_sample_inputs(host, seed=1):
@@ -431,6 +475,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end pass")
     ap.add_argument("--eager", action="store_true", help="time plain launches instead of a CUDA graph")
+    ap.add_argument("--no-upsampler", action="store_true", help="skip the whole-upsampler img/s pass")
     ap.add_argument("--images", type=int, default=8,
                     help="images per GPU (default 8; smaller only for profiling captures)")
     args = ap.parse_args()

@@ -14,6 +14,11 @@ the CPU on seeded inputs, and writes
     tests/golden/la_config1.pt    standalone config (K=9, fp32, B=1, value
                                   384x32x32, guide 64x64x64): input hashes,
                                   every 8th output channel, output checksums
+    tests/golden/model_cases.pt   the full UPLiFT upsampler (uplift/uplift.py:
+                                  537-643) of the three released variants:
+                                  per-parameter shape + sha256 under seed 0,
+                                  and small fp32 forward cases (seeded noise
+                                  replaces torch.randn in noise_and_combine)
 
 The committed fixtures pin both the CPU oracle and the CUDA kernels to the
 reference.  Nothing on the GPU side reads the reference at run time.
@@ -39,7 +44,7 @@ def load_module(name: str, path: Path):
 
 
 def tensor_sha(t: torch.Tensor) -> str:
-    return hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
+    return hashlib.sha256(t.contiguous().reshape(-1).view(torch.uint8).numpy().tobytes()).hexdigest()
 
 
 def config1_inputs():
@@ -88,6 +93,70 @@ POOL_CASES = [
     ("pool_k17_i1_bf16_hard", 1, 16, 1, 5, 6, torch.bfloat16, True),
     ("pool_k17_i2_bf16_soft", 2, 16, 1, 5, 6, torch.bfloat16, False),
 ]
+
+
+def namespace(d):
+    from types import SimpleNamespace
+    if isinstance(d, dict):
+        return SimpleNamespace(**{k: namespace(v) for k, v in d.items()})
+    if isinstance(d, list):
+        return [namespace(v) for v in d]
+    return d
+
+
+class SeededNoise:
+    """Deterministic stand-in for torch.randn inside noise_and_combine: draws
+    from its own CPU generator in call order, then moves to the device."""
+
+    def __init__(self, seed):
+        self.g = torch.Generator().manual_seed(seed)
+        self._randn = torch.randn  # the real one, even while torch.randn is patched
+
+    def __call__(self, shape, device=None, dtype=None):
+        return self._randn(list(shape), generator=self.g).to(device=device, dtype=dtype)
+
+
+MODEL_VARIANTS = {"dinov2-s14": "uplift_dinov2-s14.yaml", "dinov3-splus16": "uplift_dinov3-splus16.yaml",
+                  "sd15-vae": "uplift_sd1.5vae.yaml"}
+
+
+def model_golden(ref: Path, up):
+    import yaml
+    out = {"params": {}, "cases": []}
+    cfgs = {}
+    for variant, fname in MODEL_VARIANTS.items():
+        cfg = namespace(yaml.safe_load(open(ref / "uplift" / "configs" / fname)))
+        cfgs[variant] = cfg
+        torch.manual_seed(0)
+        model = up.UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift)
+        out["params"][variant] = {k: (list(v.shape), tensor_sha(v.detach().float()))
+                                  for k, v in model.state_dict().items() if v.dtype.is_floating_point}
+        out["params"][variant]["__keys__"] = list(model.state_dict().keys())
+    # forward cases (fp32, eval mode)
+    specs = [("dinov2-s14", 1, 56, 4, 2, None, 11), ("dinov2-s14", 2, 56, 4, 2, [30, 30], 12),
+             ("sd15-vae", 1, 32, 4, 2, None, 13)]
+    for variant, B, img_px, feat_px, iters, outsize, seed in specs:
+        cfg = cfgs[variant]
+        torch.manual_seed(0)
+        model = up.UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift).eval()
+        model.enable_iterative(iters)
+        g = torch.Generator().manual_seed(seed)
+        lo = -1.0 if variant == "sd15-vae" else 0.0
+        img = torch.rand(B, 3, img_px, img_px, generator=g) * (1 - lo) + lo
+        feats = torch.randn(B, cfg.backbone.channel, feat_px, feat_px, generator=g)
+        real_randn = torch.randn
+        noise = SeededNoise(seed + 1000)
+        try:
+            torch.randn = lambda *a, **k: noise(a[0], k.get("device"), k.get("dtype")) if a and isinstance(a[0], list) else real_randn(*a, **k)
+            with torch.no_grad():
+                y = model(img, feats, outsize)
+        finally:
+            torch.randn = real_randn
+        step = 4 if y.numel() > 200_000 else 1  # keep the fixture small: every 4th channel
+        out["cases"].append(dict(variant=variant, B=B, iters=iters, outsize=outsize, img=img, feats=feats,
+                                 noise_seed=seed + 1000, channel_step=step, out=y[:, ::step].clone()))
+        print(f"model {variant:14s} out {tuple(y.shape)}")
+    return out
 
 
 def main():
@@ -147,6 +216,10 @@ def main():
                 out_shape=list(out.shape))
     torch.save(cfg1, HERE / "la_config1.pt")
     print("config1", tuple(out.shape), cfg1["out_sum"])
+
+    mg = model_golden(ref, up)
+    mg["meta"] = meta
+    torch.save(mg, HERE / "model_cases.pt")
 
 
 if __name__ == "__main__":

@@ -1,0 +1,74 @@
+"""End-to-end parity of the upsampler (reference iteration loop around the
+fused attender) with outputs of the reference model itself (fp32, seeded
+noise), and of make_fast with the plain model."""
+import pytest
+import torch
+
+from conftest import GOLDEN, normwise_err
+from golden.make_golden import SeededNoise
+from uplift_b200 import uplift as U
+from uplift_b200.configs import get_config
+from uplift_b200.fast import make_fast
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module")
+def model_golden():
+    return torch.load(GOLDEN / "model_cases.pt", weights_only=False)
+
+
+@pytest.fixture(autouse=True)
+def no_tf32():
+    old = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = old
+
+
+def _model(variant, iters):
+    cfg = get_config(variant)
+    torch.manual_seed(0)
+    m = U.UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift).eval()
+    m.enable_iterative(iters)
+    return m.to(DEV)
+
+
+def test_upsampler_matches_reference(model_golden, cuda_lib, monkeypatch):
+    for case in model_golden["cases"]:
+        model = _model(case["variant"], case["iters"])
+        monkeypatch.setattr(U, "_randn", SeededNoise(case["noise_seed"]))
+        with torch.no_grad():
+            y = model(case["img"].to(DEV), case["feats"].to(DEV), case["outsize"])
+        y = y[:, ::case["channel_step"]].float().cpu()
+        assert y.shape == case["out"].shape
+        err = normwise_err(y, case["out"])
+        assert err <= 1e-4, (case["variant"], case["outsize"], err)
+
+
+def test_make_fast_matches_plain(model_golden, cuda_lib):
+    case = model_golden["cases"][0]  # DINOv2 arch, no final resize
+    model = _model(case["variant"], case["iters"])
+    fast = make_fast(model, compile=False, device=torch.device(DEV))
+    with torch.no_grad():
+        y_plain = model(case["img"].to(DEV), case["feats"].to(DEV))
+    y_fast = fast(case["img"].to(DEV), case["feats"].to(DEV))
+    # BatchNorm folding changes rounding only
+    assert normwise_err(y_fast, y_plain) <= 1e-4
+
+
+def test_bf16_upsampler_runs_tensor_core_path(cuda_lib):
+    from uplift_b200 import _native
+    cfg = get_config("dinov2-s14")
+    torch.manual_seed(0)
+    m = U.UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift, dtype=torch.bfloat16).eval().to(DEV)
+    m.enable_iterative(2)
+    img = torch.rand(2, 3, 112, 112, device=DEV, dtype=torch.bfloat16)
+    feats = torch.randn(2, 384, 8, 8, device=DEV, dtype=torch.bfloat16)
+    with torch.no_grad():
+        y = m(img, feats)
+    torch.cuda.synchronize()
+    assert y.shape == (2, 384, 32, 32) and torch.isfinite(y.float()).all()
+    assert _native.last_kernel() == _native.KERNEL_TENSOR_CORE
