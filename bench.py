@@ -66,7 +66,7 @@ def load_peaks():
 
 def load_traffic():
     """DRAM bytes per step from the committed ncu summary, if present."""
-    p = ROOT / "profiles" / "la_fwd_dinov2_448_b8_traffic.txt"
+    p = ROOT / "profiles" / "la_tc_kernel_dinov2_448_b8_traffic.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
