@@ -60,11 +60,12 @@ constexpr int kKSteps = kWin / 16;           // MMA-2 K steps
 constexpr int kChunk = 64;                   // channels per value / output chunk
 constexpr int kMaxC = 384;
 constexpr int kUnitChunks = 3;               // value chunks per ring unit (one accumulator half)
-constexpr int kNU = 3;                       // value ring units
+constexpr int kNU = 2;                       // value ring units
 constexpr int kLogN = 32;                    // MMA-1 N (K <= 32 logits)
 constexpr int kLogCol = kMaxC;               // TMEM column of the logit accumulators
 constexpr int kTmemCols = 512;
-constexpr int kThreads = 576;                // 18 warps
+constexpr int kThreads = 608;                // 19 warps
+constexpr int kGuideWarp = 18;               // guide-tile producer
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 
 constexpr int kVBytes = kWin * 128;          // 12 KB: 96 window px x 64 ch
@@ -78,7 +79,7 @@ constexpr int kOffV = 0;
 constexpr int kUnitBytes = kUnitChunks * kVBytes;  // 36 KB
 constexpr int kOffG = kOffV + kNU * kUnitBytes;
 constexpr int kOffStage = kOffG + 2 * kGBytes;
-constexpr int kOffW = kOffStage + 2 * kStageBytes;
+constexpr int kOffW = kOffStage + 4 * kStageBytes;  // 8 epilogue warps x 2 x 4 KB
 constexpr int kOffA2 = kOffW + kWBytes;
 constexpr int kOffBar = kOffA2 + 2 * kA2Bytes;
 constexpr int kNumBars = 2 + 2 + kNU + kNU + 2 + 2 + 2 + 2 + 2 + 2 + 1;
@@ -168,7 +169,7 @@ __device__ __forceinline__ void tma_store(const CUtensorMap* map, const void* sr
       : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -323,35 +324,44 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
   for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) ++local_tiles;
   const int half_chunks = (p.nchunks + 1) / 2;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp == 0 || warp == kGuideWarp) {
+    // ------------------------------------------------------------ producers
+    // warp 0 streams the value windows through the ring; a separate warp
+    // streams the guide tiles so that they are never queued behind a value
+    // load that waits for ring space (the logits of tile n+1 gate the MMA
+    // issue order)
     if (lane == 0) {
-      prefetch_map(&p.gmap);
-      prefetch_map(&p.vmap);
-      prefetch_map(&p.omap);
-      uint32_t vc = 0;
       bool ok = true;
-      for (int n = 0; n < local_tiles && ok; ++n) {
-        const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
-        const int s = n & 1;
-        const uint32_t ph = (n >> 1) & 1;
-        ok = mbar_wait(&g_empty[s], ph ^ 1, abort_flag, 1);
-        if (!ok) break;
-        mbar_expect_tx(&g_full[s], kGBytes);
-        tma_load(sG + s * kGBytes, &p.gmap, &g_full[s], 0, 2 * tl.cx0, 2 * tl.cy0, tl.b);
-        // value window, one ring unit per accumulator half (<= 3 chunks of
-        // 64 channels, contiguous so that one MMA spans them)
-        for (int h = 0; h < 2 && ok; ++h) {
-          const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
-          if (j0 >= j1) continue;
-          const int slot = vc % kNU;
-          ok = mbar_wait(&v_empty[slot], ((vc / kNU) & 1) ^ 1, abort_flag, 1);
+      if (warp == kGuideWarp) {
+        prefetch_map(&p.gmap);
+        for (int n = 0; n < local_tiles && ok; ++n) {
+          const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+          const int s = n & 1;
+          ok = mbar_wait(&g_empty[s], ((n >> 1) & 1) ^ 1, abort_flag, 1);
           if (!ok) break;
-          mbar_expect_tx(&v_full[slot], (j1 - j0) * kVBytes);
-          for (int j = j0; j < j1; ++j)
-            tma_load(sV + slot * kUnitBytes + (j - j0) * kVBytes, &p.vmap, &v_full[slot], j * kChunk,
-                     tl.cx0 - 2, tl.cy0 - 2, tl.b);
-          ++vc;
+          mbar_expect_tx(&g_full[s], kGBytes);
+          tma_load(sG + s * kGBytes, &p.gmap, &g_full[s], 0, 2 * tl.cx0, 2 * tl.cy0, tl.b);
+        }
+      } else {
+        prefetch_map(&p.vmap);
+        prefetch_map(&p.omap);
+        uint32_t vc = 0;
+        for (int n = 0; n < local_tiles && ok; ++n) {
+          const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+          // value window, one ring unit per accumulator half (<= 3 chunks of
+          // 64 channels, contiguous so that one MMA spans them)
+          for (int h = 0; h < 2 && ok; ++h) {
+            const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
+            if (j0 >= j1) continue;
+            const int slot = vc % kNU;
+            ok = mbar_wait(&v_empty[slot], ((vc / kNU) & 1) ^ 1, abort_flag, 1);
+            if (!ok) break;
+            mbar_expect_tx(&v_full[slot], (j1 - j0) * kVBytes);
+            for (int j = j0; j < j1; ++j)
+              tma_load(sV + slot * kUnitBytes + (j - j0) * kVBytes, &p.vmap, &v_full[slot], j * kChunk,
+                       tl.cx0 - 2, tl.cy0 - 2, tl.b);
+            ++vc;
+          }
         }
       }
       if (!ok) {  // let issued loads land before the CTA can exit
@@ -533,7 +543,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     const int q = warp & 3;
     const int h = (warp - 10) >> 2;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-    uint8_t* buf = sStage + (warp - 10) * kWarpStage;
+    uint8_t* bufs = sStage + (warp - 10) * 2 * kWarpStage;  // two staging buffers per warp
+    uint32_t jw = 0;
     const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
     for (int n = 0; n < local_tiles && j0 < j1; ++n) {
       const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
@@ -549,7 +560,9 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
           __syncwarp();
           if (lane == 0) mbar_arrive(&out_empty[h]);
         }
-        if (lane == 0) bulk_wait_read0();  // previous store from `buf` has read it
+        uint8_t* buf = bufs + (jw & 1) * kWarpStage;
+        ++jw;
+        if (lane == 0) bulk_wait_read1();  // the store issued two chunks ago has read `buf`
         __syncwarp();
         uint8_t* row = buf + lane * 128;
 #pragma unroll
