@@ -119,6 +119,14 @@ int uplift_la_last_kernel(void);
  * device; `clear` resets the word.  Returns -1 if the read failed. */
 int uplift_la_device_status(int clear);
 
+/* Testing only: fault = 1 makes the tensor-core kernel's guide producer issue
+ * no loads, so the consumers' bounded waits run out; wait_limit_ns (0 =
+ * default 2 s) caps every mbarrier wait.  fault = 0 restores normal
+ * operation.  Used to check that an expired wait is reported through
+ * uplift_la_device_status() and leaves the context usable.  No reference
+ * counterpart. */
+int uplift_la_test_hook(int fault, unsigned long long wait_limit_ns);
+
 /* Message for the last non-OK status returned on the calling thread. */
 const char* uplift_la_last_error(void);
 

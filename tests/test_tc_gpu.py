@@ -118,3 +118,25 @@ def test_policy_errors(cuda_lib):
         _run(_native.POLICY_TENSOR_CORE, guide, value, weight, bias, 17)
     out, kernel = _run(_native.POLICY_AUTO, guide, value, weight, bias, 17)
     assert kernel == _native.KERNEL_SIMT
+
+
+def test_expired_wait_is_reported_and_context_survives(cuda_lib):
+    """Failure detection without a GPU fault: the test hook makes the guide
+    producer issue no loads, so the consumers' bounded waits (limited to
+    20 ms here) run out.  The kernel must record the role in the device
+    status word, drain and exit; the context must stay usable."""
+    lib = _native.load()
+    guide, value, weight, bias = _inputs(1, 8, 16, 64, 17, torch.bfloat16, seed=21)
+    offsets, _ = neighbourhood(17)
+    assert _native.device_status(clear=True) == 0
+    _native.check(lib.uplift_la_test_hook(1, 20_000_000), "test hook")
+    try:
+        _run(_native.POLICY_TENSOR_CORE, guide, value, weight, bias, 17)  # synchronises
+        status = _native.device_status(clear=True)
+    finally:
+        lib.uplift_la_test_hook(0, 0)
+    assert status in (1, 2, 3, 4), status
+    out, kernel = _run(_native.POLICY_TENSOR_CORE, guide, value, weight, bias, 17)
+    exp = c_oracle.forward(guide, value, weight, bias, offsets)
+    assert normwise_err(out, exp) <= TC_TOL[torch.bfloat16]
+    assert _native.device_status(clear=True) == 0

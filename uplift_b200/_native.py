@@ -28,6 +28,7 @@ EXPORTED = (
     "uplift_la_set_kernel_policy",
     "uplift_la_last_kernel",
     "uplift_la_device_status",
+    "uplift_la_test_hook",
 )
 POLICY_AUTO, POLICY_SIMT, POLICY_TENSOR_CORE = 0, 1, 2
 KERNEL_SIMT, KERNEL_TENSOR_CORE = 1, 2
@@ -81,6 +82,8 @@ def load(build_if_missing: bool = False):
         lib.uplift_la_last_kernel.argtypes = []
         lib.uplift_la_device_status.restype = i
         lib.uplift_la_device_status.argtypes = [i]
+        lib.uplift_la_test_hook.restype = i
+        lib.uplift_la_test_hook.argtypes = [i, ctypes.c_ulonglong]
         _lib = lib
     return _lib
 

@@ -30,6 +30,9 @@ int tc_launch(const TcArgs& a, cudaStream_t stream);
 // -1 if the read failed.
 int tc_device_status(bool clear);
 
+// Test hook of the tensor-core kernel (see uplift_la_test_hook).
+int tc_set_test_hook(int fault, unsigned long long timeout_ns);
+
 // Record an error message for uplift_la_last_error().
 int fail(int code, const char* fmt, ...);
 

@@ -53,6 +53,10 @@ __device__ unsigned int g_tc_status;
 
 namespace tc {
 
+// Test hook state (uplift_la_test_hook): a fault mode and a wait limit.
+int g_test_fault = 0;
+uint64_t g_test_timeout_ns = 0;
+
 constexpr int kCellsY = 4, kCellsX = 8;      // cells per tile
 constexpr int kM = 128;                      // output pixels per tile (8 x 16)
 constexpr int kWinX = 12, kWin = 96;         // value window 8 x 12 (pn <= 2)
@@ -66,7 +70,7 @@ constexpr int kLogCol = kMaxC;               // TMEM column of the logit accumul
 constexpr int kTmemCols = 512;
 constexpr int kThreads = 608;                // 19 warps
 constexpr int kGuideWarp = 18;               // guide-tile producer
-constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr uint64_t kTimeoutNs = 2000000000ull;  // default limit of every mbarrier wait
 
 constexpr int kVBytes = kWin * 128;          // 12 KB: 96 window px x 64 ch
 constexpr int kGBytes = kM * 128;            // 16 KB: 128 px x 64 guide ch
@@ -100,6 +104,8 @@ struct Params {
   int res_k;            // residual channels (min(K, Cg) when conv_res, else 0)
   int hardmax;
   int margin;           // max |offset| (cells this close to a border may clamp)
+  uint64_t timeout_ns;  // limit of every mbarrier wait
+  int test_fault;       // 1: the guide producer issues no loads (tests the timeout path)
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -134,14 +140,15 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
 // Bounded wait for the phase of parity `parity` to complete.  Returns false
 // (after flagging the CTA and the device status word) on timeout, or when
 // another role of the CTA has already given up.
-__device__ __noinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, unsigned where) {
+__device__ __noinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, unsigned where,
+                                      uint64_t limit_ns) {
   if (mbar_try(b, parity)) return true;
   const uint64_t t0 = gtimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try(b, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort_flag) return false;
-      if (gtimer() - t0 > kTimeoutNs) {
+      if (gtimer() - t0 > limit_ns) {
         *abort_flag = 1;
         atomicCAS(&g_tc_status, 0u, where);
         return false;
@@ -299,7 +306,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       mbar_init(&v_empty[i], 1);
     }
     mbar_init(drain, 1);
-    *abort_flag = 0;
+    abort_flag[0] = 0;
+    abort_flag[1] = 0;  // stays 0: the flag of waits that must not be aborted
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // Projection weights in the storage type, K-major with the 128-byte swizzle
@@ -322,6 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
 
   int local_tiles = 0;
   for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) ++local_tiles;
+  const uint64_t tmo = p.timeout_ns;
   const int half_chunks = (p.nchunks + 1) / 2;
 
   if (warp == 0 || warp == kGuideWarp) {
@@ -337,8 +346,9 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
         for (int n = 0; n < local_tiles && ok; ++n) {
           const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
           const int s = n & 1;
-          ok = mbar_wait(&g_empty[s], ((n >> 1) & 1) ^ 1, abort_flag, 1);
+          ok = mbar_wait(&g_empty[s], ((n >> 1) & 1) ^ 1, abort_flag, 1, tmo);
           if (!ok) break;
+          if (p.test_fault == 1) continue;  // the guide never arrives: consumers time out
           mbar_expect_tx(&g_full[s], kGBytes);
           tma_load(sG + s * kGBytes, &p.gmap, &g_full[s], 0, 2 * tl.cx0, 2 * tl.cy0, tl.b);
         }
@@ -354,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
             const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
             if (j0 >= j1) continue;
             const int slot = vc % kNU;
-            ok = mbar_wait(&v_empty[slot], ((vc / kNU) & 1) ^ 1, abort_flag, 1);
+            ok = mbar_wait(&v_empty[slot], ((vc / kNU) & 1) ^ 1, abort_flag, 1, tmo);
             if (!ok) break;
             mbar_expect_tx(&v_full[slot], (j1 - j0) * kVBytes);
             for (int j = j0; j < j1; ++j)
@@ -379,8 +389,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       auto logits = [&](int n) -> bool {
         const int s = n & 1;
         const uint32_t ph = (n >> 1) & 1;
-        if (!mbar_wait(&g_full[s], ph, abort_flag, 2)) return false;
-        if (!mbar_wait(&log_empty[s], ph ^ 1, abort_flag, 2)) return false;
+        if (!mbar_wait(&g_full[s], ph, abort_flag, 2, tmo)) return false;
+        if (!mbar_wait(&log_empty[s], ph ^ 1, abort_flag, 2, tmo)) return false;
         tc_fence_after();
         const uint32_t aG = su32(sG + s * kGBytes);
 #pragma unroll
@@ -399,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
         }
         const int s = n & 1;
         const uint32_t ph = (n >> 1) & 1;
-        ok = mbar_wait(&a2_full[s], ph, abort_flag, 2);
+        ok = mbar_wait(&a2_full[s], ph, abort_flag, 2, tmo);
         if (!ok) break;
         tc_fence_after();
         const uint32_t aA = su32(sA2 + s * kA2Bytes);
@@ -408,11 +418,11 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
         for (int h = 0; h < 2 && ok; ++h) {
           const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
           if (j0 >= j1) continue;
-          ok = mbar_wait(&out_empty[h], (n & 1) ^ 1, abort_flag, 2);
+          ok = mbar_wait(&out_empty[h], (n & 1) ^ 1, abort_flag, 2, tmo);
           if (!ok) break;
           tc_fence_after();
           const int slot = vc % kNU;
-          ok = mbar_wait(&v_full[slot], (vc / kNU) & 1, abort_flag, 2);
+          ok = mbar_wait(&v_full[slot], (vc / kNU) & 1, abort_flag, 2, tmo);
           if (!ok) break;
           tc_fence_after();
           ++vc;
@@ -429,9 +439,10 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
         if (!ok) break;
         tc_commit(&a2_empty[s]);
       }
-      // all issued MMAs complete before TMEM can be released
+      // all issued MMAs complete before TMEM can be released (this wait
+      // ignores the abort flag: it must not be cut short by another role)
       tc_commit(drain);
-      mbar_wait(drain, 0, abort_flag, 2);
+      mbar_wait(drain, 0, abort_flag + 1, 2, tmo);
     }
   } else if (warp < 10) {
     // ------------------------------------------------------------ softmax
@@ -447,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
       const int s = n & 1;
       const uint32_t ph = (n >> 1) & 1;
-      if (!mbar_wait(&log_full[s], ph, abort_flag, 3)) break;
+      if (!mbar_wait(&log_full[s], ph, abort_flag, 3, tmo)) break;
       tc_fence_after();
       uint32_t r[32];
       tc_ld32(lane_base + kLogCol + kLogN * s, r);
@@ -455,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&log_empty[s]);
-      if (!mbar_wait(&g_full[s], ph, abort_flag, 3)) break;
+      if (!mbar_wait(&g_full[s], ph, abort_flag, 3, tmo)) break;
 
       float lg[K];
 #pragma unroll
@@ -520,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
           }
         }
       }
-      if (!mbar_wait(&a2_empty[s], ph ^ 1, abort_flag, 3)) break;
+      if (!mbar_wait(&a2_empty[s], ph ^ 1, abort_flag, 3, tmo)) break;
       // row i of A (K-major, no swizzle: 8x16-byte core matrices; 8-row
       // groups kA2Sbo apart, 8-column groups 128 B apart)
       uint8_t* arow = sA2 + s * kA2Bytes + (i >> 3) * kA2Sbo + (i & 7) * 16;
@@ -548,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
     for (int n = 0; n < local_tiles && j0 < j1; ++n) {
       const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
-      if (!mbar_wait(&out_full[h], n & 1, abort_flag, 4)) break;
+      if (!mbar_wait(&out_full[h], n & 1, abort_flag, 4, tmo)) break;
       tc_fence_after();
       for (int j = j0; j < j1; ++j) {
         uint32_t r[64];
@@ -658,6 +669,13 @@ int launch_k(const Params& p, int K, int dev, int grid, cudaStream_t stream) {
 
 }  // namespace tc
 
+int tc_set_test_hook(int fault, unsigned long long timeout_ns) {
+  if (fault < 0 || fault > 1) return fail(UPLIFT_LA_ERR_ARG, "unknown test fault %d", fault);
+  tc::g_test_fault = fault;
+  tc::g_test_timeout_ns = timeout_ns;
+  return UPLIFT_LA_OK;
+}
+
 int tc_device_status(bool clear) {
   unsigned int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_status, sizeof(v));
@@ -720,6 +738,8 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
   if (nt >= (1ll << 31)) return fail(UPLIFT_LA_ERR_SHAPE, "too many tiles");
   p.num_tiles = (int)nt;
   p.res_k = a.conv_res ? std::min(a.K, a.Cg) : 0;
+  p.timeout_ns = g_test_timeout_ns != 0 ? g_test_timeout_ns : kTimeoutNs;
+  p.test_fault = g_test_fault;
   p.hardmax = a.hardmax;
   p.margin = margin;
   int dev = 0;

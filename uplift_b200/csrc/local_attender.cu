@@ -637,6 +637,10 @@ int uplift_la_last_kernel(void) { return ula::g_last_kernel; }
 
 int uplift_la_device_status(int clear) { return ula::tc_device_status(clear != 0); }
 
+int uplift_la_test_hook(int fault, unsigned long long wait_limit_ns) {
+  return ula::tc_set_test_hook(fault, wait_limit_ns);
+}
+
 const char* uplift_la_last_error(void) { return ula::g_err; }
 
 const char* uplift_la_status_string(int status) {
