@@ -72,3 +72,25 @@ def test_bf16_upsampler_runs_tensor_core_path(cuda_lib):
     torch.cuda.synchronize()
     assert y.shape == (2, 384, 32, 32) and torch.isfinite(y.float()).all()
     assert _native.last_kernel() == _native.KERNEL_TENSOR_CORE
+
+
+def test_low_mem_equals_parallel_and_bf16_iterates(cuda_lib):
+    """DINOv3-S+/16 architecture, bf16: low_mem=True gives the same output as
+    the parallel path (the fused kernel never materialises the K-fold
+    tensor, so the flag only exists for API compatibility) and the model runs
+    for iters > 1 (the reference's low_mem returns fp32 there and the next
+    bf16 conv fails, uplift/uplift.py:840)."""
+    cfg = get_config("dinov3-splus16")
+    outs = []
+    for low_mem in (False, True):
+        torch.manual_seed(0)
+        m = U.UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift, dtype=torch.bfloat16,
+                     low_mem=low_mem).eval().to(DEV)
+        m.enable_iterative(3)
+        g = torch.Generator().manual_seed(5)
+        img = torch.rand(2, 3, 128, 128, generator=g).to(DEV, torch.bfloat16)
+        feats = torch.randn(2, 384, 8, 8, generator=g).to(DEV, torch.bfloat16)
+        with torch.no_grad():
+            outs.append(m(img, feats))
+    assert outs[0].shape == (2, 384, 64, 64) and outs[0].dtype == torch.bfloat16
+    assert torch.equal(outs[0], outs[1])

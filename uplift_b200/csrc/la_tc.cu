@@ -310,6 +310,16 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     abort_flag[1] = 0;  // stays 0: the flag of waits that must not be aborted
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)), "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  // Programmatic dependent launch: everything above touches no global
+  // memory, so it overlaps the tail of the previous kernel in the stream;
+  // nothing below may read inputs before that kernel has completed.  The
+  // next kernel may start its own prologue as soon as SMs free up.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
   // Projection weights in the storage type, K-major with the 128-byte swizzle
   // (row n = logit n, 64 guide channels per 128-byte row).
   for (int idx = tid; idx < kLogN * 64; idx += kThreads) {
@@ -319,10 +329,6 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
   }
   for (int k = tid; k < kLogN; k += kThreads) sBias[k] = (p.bias != nullptr && k < K) ? p.bias[k] : 0.f;
   fence_proxy_async();  // sW is read by the tensor core (async proxy)
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)), "r"(kTmemCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -648,9 +654,18 @@ int launch_t(const Params& p, int dev, int grid, cudaStream_t stream) {
     if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  cudaError_t e;
-  fn<<<grid, kThreads, kSmemBytes, stream>>>(p);
-  e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "tensor-core kernel launch: %s", cudaGetErrorString(e));
   return UPLIFT_LA_OK;
 }
