@@ -88,7 +88,7 @@ class OptimizedUPLiFT(nn.Module):
             ex_feats = enc_feats
             steps.append(x)
         if outsize is not None:
-            return F.interpolate(x, size=outsize, mode="bilinear", align_corners=False)
+            return _resize_bilinear(x, outsize)
         if m.return_all_steps:
             return steps
         return x
@@ -126,6 +126,21 @@ class OptimizedUPLiFT(nn.Module):
                 module[idx] = child
             while len(module) > len(out):
                 del module[len(out)]
+
+
+_INT_MAX = 2**31 - 1
+
+
+def _resize_bilinear(x, size):
+    """F.interpolate(bilinear, align_corners=False), split along the batch
+    when the input or output exceeds the 2^31-element limit of torch's
+    channels_last bilinear kernel (e.g. 8 x 384 x 1168^2)."""
+    out_numel = x.shape[0] * x.shape[1] * size[0] * size[1]
+    if max(x.numel(), out_numel) <= _INT_MAX or x.shape[0] == 1:
+        return F.interpolate(x, size=size, mode="bilinear", align_corners=False)
+    per = max(1, _INT_MAX // max(x[0].numel(), out_numel // x.shape[0]))
+    return torch.cat([F.interpolate(x[i:i + per], size=size, mode="bilinear", align_corners=False)
+                      for i in range(0, x.shape[0], per)], dim=0)
 
 
 def _warmup(fast: OptimizedUPLiFT, image_size: int, device: torch.device):
