@@ -41,6 +41,23 @@ def neighbourhood(num_connected: int):
     return [tuple(o) for o in offsets], pn
 
 
+def _fp32_projection(owner, conv1, K):
+    """conv1's weight [K, Cg] and bias [K] in fp32 for the kernel, converted
+    once and cached on `owner` until the parameters change (checked by data
+    pointer and version counter); under torch.compile the raw parameters are
+    passed and converted inside the op."""
+    w, b = conv1.weight, conv1.bias
+    if torch.compiler.is_compiling():
+        return w, b
+    key = (w.data_ptr(), w._version, w.dtype, w.device, None if b is None else (b.data_ptr(), b._version))
+    if key != owner._proj_key:
+        wf = w.detach().to(torch.float32).reshape(K, -1).contiguous()
+        bf = None if b is None else b.detach().to(torch.float32).contiguous()
+        owner._proj = (wf, bf)
+        owner._proj_key = key
+    return owner._proj
+
+
 class LocalAttender(nn.Module):
     """Local-attention pooling of a coarse value map guided by a fine guide map.
 
@@ -89,17 +106,7 @@ class LocalAttender(nn.Module):
         return torch.stack(views, dim=2)
 
     def _projection(self):
-        w, b = self.conv1.weight, self.conv1.bias
-        if torch.compiler.is_compiling():
-            return w, b
-        key = (w.data_ptr(), w._version, w.dtype, w.device,
-               None if b is None else (b.data_ptr(), b._version))
-        if key != self._proj_key:
-            wf = w.detach().to(torch.float32).reshape(self.num_connected, -1).contiguous()
-            bf = None if b is None else b.detach().to(torch.float32).contiguous()
-            self._proj = (wf, bf)
-            self._proj_key = key
-        return self._proj
+        return _fp32_projection(self, self.conv1, self.num_connected)
 
     def forward(self, guide, value, hardmax=False):
         w, b = self._projection()
@@ -139,7 +146,10 @@ class AttenderWrapper(nn.Module):
         self.num_connected = attender.num_connected
         self.offsets = attender.offsets
         self.pn = attender.pn
+        self._proj_key = None
+        self._proj = None
 
     def forward(self, guide, value, hardmax=False):
-        return ops.local_attender(guide, value, self.conv1.weight, self.conv1.bias, self.offsets,
-                                  self.pn, conv_res=self.conv_res, hardmax=hardmax)
+        w, b = _fp32_projection(self, self.conv1, self.num_connected)
+        return ops.local_attender(guide, value, w, b, self.offsets, self.pn,
+                                  conv_res=self.conv_res, hardmax=hardmax)

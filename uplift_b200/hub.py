@@ -8,6 +8,8 @@ available; `pretrained=False` builds a random-init model.
 """
 from __future__ import annotations
 
+import torch
+
 from .configs import VARIANTS, get_config
 from .uplift import UPLiFT
 
@@ -36,8 +38,7 @@ def load_model(variant: str, pretrained: bool = True, include_extractor: bool = 
             "load with include_extractor=False and pass backbone features to the model")
     cfg = get_config(variant)
     model = UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift,
-                   dtype=kwargs.pop("dtype", None) or __import__("torch").float32,
-                   low_mem=kwargs.pop("low_mem", False))
+                   dtype=kwargs.pop("dtype", torch.float32), low_mem=kwargs.pop("low_mem", False))
     if "iters" in kwargs:
         model.enable_iterative(kwargs.pop("iters"))
     if pretrained:
