@@ -25,3 +25,25 @@ def test_local_attender_compiles_fullgraph(cuda_lib):
         ref = la(guide, value)
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+def test_make_fast_compiled_matches_plain(cuda_lib):
+    """make_fast with torch.compile (BN folding, channels_last, compiled
+    iteration loop with the fused attender inside) matches the plain model."""
+    from uplift_b200 import uplift as U
+    from uplift_b200.configs import get_config
+    from uplift_b200.fast import make_fast
+    cfg = get_config("dinov2-s14")
+    torch.manual_seed(0)
+    m = U.UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift, dtype=torch.bfloat16).eval().to(DEV)
+    m.enable_iterative(2)
+    g = torch.Generator().manual_seed(3)
+    img = torch.rand(2, 3, 112, 112, generator=g).to(DEV, torch.bfloat16)
+    feats = torch.randn(2, 384, 8, 8, generator=g).to(DEV, torch.bfloat16)
+    fast = make_fast(m, compile=True, compile_mode="default", warmup=False, device=torch.device(DEV))
+    with torch.no_grad():
+        ref = m(img, feats)
+    out = fast(img, feats)
+    torch.cuda.synchronize()
+    err = ((out.float() - ref.float()).abs().max() / ref.float().abs().max()).item()
+    assert out.shape == ref.shape and err <= 2e-2, err  # bf16 convs, folded BatchNorm
