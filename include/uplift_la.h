@@ -97,12 +97,14 @@ int uplift_la_pool(const void* logits, const int64_t logits_strides[4],
                    int dtype, int hardmax, void* stream);
 
 /* Kernel selection for uplift_la_forward (process-wide; default AUTO).
- * AUTO picks the tensor-core kernel (tcgen05 MMA, TMEM accumulators, TMA)
- * when it applies -- bf16/fp16 storage, I = 2, Cg = 64, C a multiple of 64
- * up to 384, 16-byte aligned tensors -- and the CUDA-core kernel otherwise;
- * SIMT always uses the CUDA-core kernel; TENSOR_CORE makes ineligible
- * problems fail with UPLIFT_LA_ERR_SHAPE instead of falling back.  No
- * reference counterpart (the reference has a single Triton kernel family). */
+ * AUTO picks a tensor-core kernel (tcgen05 MMA, TMEM accumulators, TMA)
+ * when one applies -- bf16/fp16 storage, I = 2, Cg = 64, C a multiple of 64
+ * up to 384; or fp32 storage, I = 2, Cg a multiple of 32 in 64..512, C a
+ * multiple of 4 up to 32 (the wide-guide split-bf16 projection); 16-byte
+ * aligned tensors -- and the CUDA-core kernel otherwise; SIMT always uses
+ * the CUDA-core kernel; TENSOR_CORE makes ineligible problems fail with
+ * UPLIFT_LA_ERR_SHAPE instead of falling back.  No reference counterpart
+ * (the reference has a single Triton kernel family). */
 #define UPLIFT_LA_POLICY_AUTO        0
 #define UPLIFT_LA_POLICY_SIMT        1
 #define UPLIFT_LA_POLICY_TENSOR_CORE 2
@@ -111,15 +113,17 @@ int uplift_la_set_kernel_policy(int policy);
 /* Kernel launched by the last successful call on the calling thread. */
 #define UPLIFT_LA_KERNEL_SIMT        1
 #define UPLIFT_LA_KERNEL_TENSOR_CORE 2
+#define UPLIFT_LA_KERNEL_SIMT_STAGED 3  /* CUDA-core kernel, guide staged in shared memory */
+#define UPLIFT_LA_KERNEL_TENSOR_CORE_WIDE 4  /* fp32, wide guide: split-bf16 tensor-core projection */
 int uplift_la_last_kernel(void);
 
-/* Device status word of the tensor-core kernel: 0 when every launch so far
- * completed its pipeline, else the role (1 producer, 2 MMA, 3 softmax,
- * 4 epilogue) whose bounded wait expired first.  Synchronises with the
- * device; `clear` resets the word.  Returns -1 if the read failed. */
+/* Device status word of the tensor-core kernels: 0 when every launch so far
+ * completed its pipeline, else the role (1 producer, 2 MMA, 3 softmax or
+ * split, 4 epilogue) whose bounded wait expired first.  Synchronises with
+ * the device; `clear` resets the word.  Returns -1 if the read failed. */
 int uplift_la_device_status(int clear);
 
-/* Testing only: fault = 1 makes the tensor-core kernel's guide producer issue
+/* Testing only: fault = 1 makes the tensor-core kernels' guide producers issue
  * no loads, so the consumers' bounded waits run out; wait_limit_ns (0 =
  * default 2 s) caps every mbarrier wait.  fault = 0 restores normal
  * operation.  Used to check that an expired wait is reported through

@@ -6,7 +6,7 @@ import torch
 from conftest import TOL, dtype_of, normwise_err
 from oracle import c_oracle
 from oracle import local_attender_oracle as lao
-from uplift_b200 import ops
+from uplift_b200 import _native, ops
 from uplift_b200.attender import FusedLocalAttender, LocalAttender, neighbourhood
 
 pytestmark = pytest.mark.gpu
@@ -57,6 +57,8 @@ def test_golden_against_double_oracle(golden_cases, cuda_lib):
         exp = c_oracle.forward(case["guide"], case["value"], case["weight"], case["bias"],
                                case["offsets"], conv_res=case["conv_res"])
         tol = {torch.float32: 1e-5, torch.bfloat16: 4e-3, torch.float16: 5e-4}[dt]
+        if _native.last_kernel() == _native.KERNEL_TENSOR_CORE_WIDE:
+            tol = 3e-5  # two-term bf16 split of the fp32 projection (~2^-17 per product)
         assert normwise_err(out, exp) <= tol, (case["name"], normwise_err(out, exp))
 
 

@@ -100,7 +100,7 @@ def test_tc_full_size_vs_simt(cuda_lib):
     guide, value, weight, bias = _inputs(8, 256, 256, 384, 17, torch.bfloat16, seed=9)
     tc, k1 = _run(_native.POLICY_TENSOR_CORE, guide, value, weight, bias, 17)
     simt, k2 = _run(_native.POLICY_SIMT, guide, value, weight, bias, 17)
-    assert (k1, k2) == (_native.KERNEL_TENSOR_CORE, _native.KERNEL_SIMT)
+    assert k1 == _native.KERNEL_TENSOR_CORE and k2 in _native.KERNELS_CUDA_CORE
     assert normwise_err(tc, simt.float()) <= 1e-2
     offsets, pn = neighbourhood(17)
     for b, r0 in ((5, 0), (2, 120), (7, 252)):
@@ -117,7 +117,7 @@ def test_policy_errors(cuda_lib):
     with pytest.raises(ValueError, match="tensor-core kernel required"):
         _run(_native.POLICY_TENSOR_CORE, guide, value, weight, bias, 17)
     out, kernel = _run(_native.POLICY_AUTO, guide, value, weight, bias, 17)
-    assert kernel == _native.KERNEL_SIMT
+    assert kernel in _native.KERNELS_CUDA_CORE
 
 
 def test_expired_wait_is_reported_and_context_survives(cuda_lib):

@@ -31,7 +31,8 @@ EXPORTED = (
     "uplift_la_test_hook",
 )
 POLICY_AUTO, POLICY_SIMT, POLICY_TENSOR_CORE = 0, 1, 2
-KERNEL_SIMT, KERNEL_TENSOR_CORE = 1, 2
+KERNEL_SIMT, KERNEL_TENSOR_CORE, KERNEL_SIMT_STAGED, KERNEL_TENSOR_CORE_WIDE = 1, 2, 3, 4
+KERNELS_CUDA_CORE = (KERNEL_SIMT, KERNEL_SIMT_STAGED)
 
 _lib = None
 _lock = threading.Lock()

@@ -42,7 +42,7 @@ def is_stale() -> bool:
     if not lib.exists():
         return True
     t = lib.stat().st_mtime
-    deps = sources() + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    deps = sources() + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))
     return any(d.stat().st_mtime > t for d in deps)
 
 

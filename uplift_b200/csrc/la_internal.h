@@ -1,8 +1,9 @@
 // Internal interface between the C-ABI front end (local_attender.cu) and
-// the tensor-core kernel (la_tc.cu).  Not part of the public ABI.
+// the tensor-core kernels (la_tc.cu, la_tcw.cu).  Not part of the public ABI.
 #pragma once
 
 #include <stdint.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace ula {
@@ -30,10 +31,24 @@ int tc_launch(const TcArgs& a, cudaStream_t stream);
 // -1 if the read failed.
 int tc_device_status(bool clear);
 
-// Test hook of the tensor-core kernel (see uplift_la_test_hook).
+// Test hook of the tensor-core kernels (see uplift_la_test_hook) and its
+// current settings.
 int tc_set_test_hook(int fault, unsigned long long timeout_ns);
+int tc_test_fault();
+unsigned long long tc_test_timeout_ns();
+
+// Tensor-core projection for wide fp32 guides (la_tcw.cu): eligibility,
+// launch and status word, as above.
+bool tcw_eligible(const TcArgs& a, const char** why);
+int tcw_launch(const TcArgs& a, cudaStream_t stream);
+int tcw_device_status(bool clear);
 
 // Record an error message for uplift_la_last_error().
 int fail(int code, const char* fmt, ...);
+
+// NHWC 4-D TMA map with the 128-byte swizzle (dims {C, W, H, B}, strides in
+// elements of `es` bytes).
+int tc_make_map(CUtensorMap* map, CUtensorMapDataType dt, int es, const void* base, int C, int W, int H, int B,
+                int64_t s_w, int64_t s_h, int64_t s_b, int box_c, int box_w, int box_h);
 
 }  // namespace ula

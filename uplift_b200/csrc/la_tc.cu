@@ -44,6 +44,7 @@
 
 #include "uplift_la.h"
 #include "la_internal.h"
+#include "la_tc_common.h"
 
 namespace ula {
 
@@ -108,120 +109,10 @@ struct Params {
   int test_fault;       // 1: the guide producer issues no loads (tests the timeout path)
 };
 
-// ------------------------------------------------------------ PTX helpers
-__device__ __forceinline__ uint32_t su32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint64_t gtimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count));
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(su32(b)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait for the phase of parity `parity` to complete.  Returns false
-// (after flagging the CTA and the device status word) on timeout, or when
-// another role of the CTA has already given up.
-__device__ __noinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, unsigned where,
-                                      uint64_t limit_ns) {
-  if (mbar_try(b, parity)) return true;
-  const uint64_t t0 = gtimer();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try(b, parity)) return true;
-    if ((it & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (gtimer() - t0 > limit_ns) {
-        *abort_flag = 1;
-        atomicCAS(&g_tc_status, 0u, where);
-        return false;
-      }
-    }
-  }
-}
-__device__ __forceinline__ void named_bar(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
-      ::"r"(su32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)),
-        "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-__device__ __forceinline__ void tma_store(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
-      ::"l"(reinterpret_cast<uint64_t>(map)), "r"(su32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar)) : "memory");
-}
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
-      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
-      : "memory");
-}
-__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-// 32 lanes x 32 consecutive 32-bit columns: thread (lane) gets its row.
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-
-// Shared-memory matrix descriptors (tcgen05 "matrix descriptor": start
-// address >> 4 in bits 0-13, leading byte offset >> 4 in 16-29, stride
-// byte offset >> 4 in 32-45, version 1 in 46-47, layout type in 61-63).
-__device__ __forceinline__ uint64_t mdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
-}
-constexpr uint32_t kLayoutNone = 0, kLayoutSw128 = 2;
-
-// Instruction descriptor, kind::f16: fp32 accumulate, A/B type (0 = f16,
-// 1 = bf16), K-major A, B major per flag, N >> 3 at bit 17, M >> 4 at bit 24.
-__host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_fmt, uint32_t b_mn_major, uint32_t m, uint32_t n) {
-  return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (b_mn_major << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+// Bounded mbarrier wait recording expiries in this kernel's status word.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, unsigned where,
+                                          uint64_t limit_ns) {
+  return mbar_wait_status(b, parity, abort_flag, where, limit_ns, &g_tc_status);
 }
 
 template <typename T> struct Store;
@@ -629,13 +520,16 @@ EncodeTiled encode_fn() {
   return fn;
 }
 
-// NHWC 4-D map: dims {C, W, H, B}, element strides in elements.
-int make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int C, int W, int H, int B,
-             int64_t s_w, int64_t s_h, int64_t s_b, int box_c, int box_w, int box_h) {
-  EncodeTiled enc = encode_fn();
+}  // namespace tc
+
+// NHWC 4-D map with the 128-byte swizzle: dims {C, W, H, B}, strides in
+// elements of `es` bytes.
+int tc_make_map(CUtensorMap* map, CUtensorMapDataType dt, int es, const void* base, int C, int W, int H, int B,
+                int64_t s_w, int64_t s_h, int64_t s_b, int box_c, int box_w, int box_h) {
+  tc::EncodeTiled enc = tc::encode_fn();
   if (enc == nullptr) return fail(UPLIFT_LA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)B};
-  const cuuint64_t strides[3] = {(cuuint64_t)s_w * 2, (cuuint64_t)s_h * 2, (cuuint64_t)s_b * 2};
+  const cuuint64_t strides[3] = {(cuuint64_t)s_w * es, (cuuint64_t)s_h * es, (cuuint64_t)s_b * es};
   const cuuint32_t box[4] = {(cuuint32_t)box_c, (cuuint32_t)box_w, (cuuint32_t)box_h, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -643,6 +537,8 @@ int make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int C, 
   if (r != CUDA_SUCCESS) return fail(UPLIFT_LA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return UPLIFT_LA_OK;
 }
+
+namespace tc {
 
 template <typename T, int K>
 int launch_t(const Params& p, int dev, int grid, cudaStream_t stream) {
@@ -691,6 +587,9 @@ int tc_set_test_hook(int fault, unsigned long long timeout_ns) {
   return UPLIFT_LA_OK;
 }
 
+int tc_test_fault() { return tc::g_test_fault; }
+unsigned long long tc_test_timeout_ns() { return tc::g_test_timeout_ns; }
+
 int tc_device_status(bool clear) {
   unsigned int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_status, sizeof(v));
@@ -732,9 +631,9 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
   Params p;
   memset(&p, 0, sizeof(p));
   const CUtensorMapDataType dt = a.dtype == UPLIFT_LA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  int rc = make_map(&p.gmap, dt, a.guide, a.Cg, 2 * a.W, 2 * a.H, a.B, a.g_w, a.g_h, a.g_b, 64, 16, 8);
-  if (rc == UPLIFT_LA_OK) rc = make_map(&p.vmap, dt, a.value, a.C, a.W, a.H, a.B, a.v_w, a.v_h, a.v_b, 64, kWinX, 8);
-  if (rc == UPLIFT_LA_OK) rc = make_map(&p.omap, dt, a.out, a.C, 2 * a.W, 2 * a.H, a.B, a.o_w, a.o_h, a.o_b, 64, 16, 2);
+  int rc = tc_make_map(&p.gmap, dt, 2, a.guide, a.Cg, 2 * a.W, 2 * a.H, a.B, a.g_w, a.g_h, a.g_b, 64, 16, 8);
+  if (rc == UPLIFT_LA_OK) rc = tc_make_map(&p.vmap, dt, 2, a.value, a.C, a.W, a.H, a.B, a.v_w, a.v_h, a.v_b, 64, kWinX, 8);
+  if (rc == UPLIFT_LA_OK) rc = tc_make_map(&p.omap, dt, 2, a.out, a.C, 2 * a.W, 2 * a.H, a.B, a.o_w, a.o_h, a.o_b, 64, 16, 2);
   if (rc != UPLIFT_LA_OK) return rc;
   p.weight = a.weight;
   p.bias = a.bias;

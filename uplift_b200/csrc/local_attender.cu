@@ -21,7 +21,19 @@
 //        k it loads one value vector (coalesced NHWC, read-only path) and
 //        accumulates CPT children with packed fp32 FMA (FFMA2).
 //   The grid is persistent (a multiple of the SM count); the projection
-//   weights are staged in shared memory once per CTA.
+//   weights are staged in shared memory once per CTA.  When there are fewer
+//   tiles than resident CTAs, each tile is split into channel slices
+//   (phase A is repeated per slice, phase B covers the slice's channels).
+//
+// Staged variant (STAGED, guide rows 16-byte aligned): phase A streams the
+// guide through a cp.async ring of 128-byte-per-pixel chunks in shared
+// memory (coalesced 128-byte row segments instead of one 16-byte load per
+// pixel per thread) and computes the projection register-blocked: a thread
+// owns P pixels x all K logits for a quarter (or half) of each chunk's
+// channels, with packed FMAs over channel pairs; the partial logits are
+// reduced across warps through the (then idle) ring.  For wide guides
+// (SD-VAE: Cg = 512) the projection dominates and this path is what keeps
+// the kernel near the HBM roofline.
 //
 // Storage is NHWC (channel stride 1); accumulation is fp32 throughout.
 
@@ -57,6 +69,7 @@ struct Params {
   int units_per_cell;    // I*I / CPT
   int num_units;         // B*H*W*units_per_cell
   int num_tiles;
+  int cslices;           // channel slices per tile (work items = num_tiles * cslices)
   int8_t dy[kMaxK];
   int8_t dx[kMaxK];
 };
@@ -130,6 +143,38 @@ __device__ __forceinline__ uint4 ldg_nc16(const void* p) {
 
 __device__ __forceinline__ int clampi(int v, int lo, int hi) { return min(max(v, lo), hi); }
 
+__device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+
+// 16-byte global -> shared copy, zero-filled when src_bytes == 0 (no read).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+// Staged guide ring: kStages slots of kTilePix rows x kRowBytes.  Row r of a
+// slot holds 8 16-byte units of one pixel's channel chunk; unit u is stored
+// at slot (u ^ (r & 7)) so that 8 consecutive pixels reading the same unit
+// hit 8 different bank groups.
+constexpr int kStages = 4;
+constexpr int kRowBytes = 128;
+constexpr int kStageBytes = kTilePix * kRowBytes;
+
+// Register blocking of the staged projection: P pixels per thread (two for
+// K <= 17, one for K = 25 to bound the accumulators), kWarps / NCS groups of
+// 32*P pixels, NCS channel splits (warps sharing pixels, distinct units).
+template <int K>
+struct StagedMap {
+  static constexpr int P = K <= 17 ? 2 : 1;
+  static constexpr int NPG = kTilePix / (32 * P);
+  static constexpr int NCS = (kThreads / 32) / NPG;
+  static constexpr int UPT = 8 / NCS;  // units per thread per chunk
+  static_assert(NPG * NCS == kThreads / 32 && UPT * NCS == 8, "staged mapping");
+};
+
 // Shared-memory layout (floats / ints), sized on the host by smem_bytes().
 template <int K, int CPT>
 struct Smem {
@@ -138,24 +183,55 @@ struct Smem {
   // offsets in 4-byte words
   static constexpr int kP = 0;                               // [units][K][CPT] fp32 weights
   static constexpr int kNbr = kP + kUnits * K * CPT;         // [units][K] int32 value offsets
-  static constexpr int kOut = (kNbr + kUnits * K + 1) & ~1;  // [units][CPT] int64 out offsets
-  static constexpr int kBias = kOut + 2 * kUnits * CPT;      // [kKP]
+  static constexpr int kOut = (kNbr + kUnits * K + 1) & ~1;  // [units][CPT] int64 out offsets, then
+                                                             // [kTilePix] int64 guide-row offsets (staged)
+  static constexpr int kBias = kOut + 4 * kUnits * CPT;      // [kKP] (after out and staged guide-row offsets)
   static constexpr int kW = (kBias + kKP + 3) & ~3;          // [Cg][kKP] (projection only)
   static size_t bytes(int Cg, bool from_logits) {
     return 4 * (size_t)(kW + (from_logits ? 0 : Cg * kKP));
   }
+  // staged variant: weights [Cgp / VE][K][VE] (Cgp = Cg rounded up to whole
+  // chunks), then the guide ring (also holds the [NCS][K][kTilePix]
+  // cross-warp reduction, which is smaller)
+  __host__ __device__ static size_t ring_offset(int Cgp) { return ((4 * (size_t)(kW + Cgp * K)) + 127) & ~(size_t)127; }
+  static size_t staged_bytes(int Cgp) { return ring_offset(Cgp) + (size_t)kStages * kStageBytes; }
+  static_assert(StagedMap<K>::NCS * K * kTilePix * 4 <= kStages * kStageBytes, "reduction fits the ring");
 };
 
-template <typename T, int K, int CPT, bool VEC>
-__global__ void __launch_bounds__(kThreads)
-la_fwd_kernel(const __grid_constant__ Params p) {
+// Output pixel `pix` of tile `tile` -> (batch, parent cell, pixel); false
+// past the last unit.
+template <int CPT>
+__device__ __forceinline__ bool pixel_coords(const Params& p, int tile, int pix,
+                                             int& b, int& cy, int& cx, int& y, int& x) {
+  constexpr int NU = kTilePix / CPT;
+  const int u = pix / CPT, t = pix - u * CPT;
+  const int unit = tile * NU + u;
+  if (unit >= p.num_units) return false;
+  const int sub = unit % p.units_per_cell;
+  const int cell = unit / p.units_per_cell;
+  cx = cell % p.W;
+  const int rest = cell / p.W;
+  cy = rest % p.H;
+  b = rest / p.H;
+  const int ch = sub * CPT + t;
+  const int ci = ch / p.I;
+  y = cy * p.I + ci;
+  x = cx * p.I + (ch - ci * p.I);
+  return true;
+}
+
+template <typename T, int K, int CPT, bool VEC, bool STAGED>
+__device__ __forceinline__ void la_fwd_body(const Params& p) {
   using E = Elem<T>;
   using S = Smem<K, CPT>;
+  using SM = StagedMap<K>;
   constexpr int KP = S::kKP;
   constexpr int NU = S::kUnits;
   constexpr int V = VEC ? E::kVec : 1;
+  constexpr int VE = E::kVec;               // elements per 16-byte unit
+  constexpr int CH = kRowBytes / sizeof(T);  // channels per staged chunk
 
-  extern __shared__ __align__(16) float smem[];
+  extern __shared__ __align__(128) float smem[];
   float* s_p = smem + S::kP;
   int* s_nbr = reinterpret_cast<int*>(smem + S::kNbr);
   long long* s_out = reinterpret_cast<long long*>(smem + S::kOut);
@@ -163,19 +239,35 @@ la_fwd_kernel(const __grid_constant__ Params p) {
   float* s_w = smem + S::kW;
 
   const int tid = threadIdx.x;
+  const int nchunks = (p.Cg + CH - 1) / CH;
+  char* ring = reinterpret_cast<char*>(smem) + (STAGED ? S::ring_offset(nchunks * CH) : 0);
 
   // Stage the projection once per CTA.  The residual guide[:, :K] of
   // residual_auto (uplift/uplift.py:26-39) is linear in the guide, so it is
   // folded into the weights: logit = (W + E) g + b with E[k][c] = (k == c).
   if (!p.from_logits) {
-    for (int i = tid; i < p.Cg * KP; i += kThreads) {
-      const int c = i / KP, k = i - c * KP;
-      float w = 0.f;
-      if (k < K) {
-        w = p.weight[(size_t)k * p.Cg + c];
-        if (p.conv_res && k == c) w += 1.f;
+    if constexpr (STAGED) {
+      // [c / VE][k][c % VE], zero past Cg
+      const int n = nchunks * CH * K;
+      for (int i = tid; i < n; i += kThreads) {
+        const int e = i % VE, k = (i / VE) % K, c = (i / (VE * K)) * VE + e;
+        float w = 0.f;
+        if (c < p.Cg) {
+          w = p.weight[(size_t)k * p.Cg + c];
+          if (p.conv_res && k == c) w += 1.f;
+        }
+        s_w[i] = w;
       }
-      s_w[i] = w;
+    } else {
+      for (int i = tid; i < p.Cg * KP; i += kThreads) {
+        const int c = i / KP, k = i - c * KP;
+        float w = 0.f;
+        if (k < K) {
+          w = p.weight[(size_t)k * p.Cg + c];
+          if (p.conv_res && k == c) w += 1.f;
+        }
+        s_w[i] = w;
+      }
     }
     for (int k = tid; k < KP; k += kThreads)
       s_bias[k] = (p.bias != nullptr && k < K) ? p.bias[k] : 0.f;
@@ -186,35 +278,110 @@ la_fwd_kernel(const __grid_constant__ Params p) {
   const T* __restrict__ vbase = static_cast<const T*>(p.value);
   T* __restrict__ obase = static_cast<T*>(p.out);
 
-  for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+  const int num_work = p.num_tiles * p.cslices;
+  for (int work = blockIdx.x; work < num_work; work += gridDim.x) {
+    const int tile = work / p.cslices;
+    const int slice = work - tile * p.cslices;
     __syncthreads();  // previous tile's phase B is done with shared memory
+
+    // ------------------------------------------------- phase A, staged guide
+    if constexpr (STAGED) {
+      // guide row offset of every pixel of the tile (-1: past the end)
+      long long* s_grow = s_out + NU * CPT;
+      if (tid < kTilePix) {
+        int b, cy, cx, y, x;
+        s_grow[tid] = pixel_coords<CPT>(p, tile, tid, b, cy, cx, y, x) ? b * p.g_b + y * p.g_h + x * p.g_w : -1;
+      }
+      __syncthreads();
+      // copy roles: thread copies unit (tid & 7) of pixel rows (tid >> 3) + 32 j
+      const int cu = tid & 7;
+      auto issue = [&](int chunk, int slot) {
+        const int c0 = chunk * CH + cu * VE;
+        const uint32_t sbase = smem_u32(ring + slot * kStageBytes);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int r = (tid >> 3) + 32 * j;
+          const long long off = s_grow[r];
+          const bool ok = off >= 0 && c0 < p.Cg;
+          cp_async16(sbase + r * kRowBytes + ((cu ^ (r & 7)) << 4), ok ? (const void*)(gbase + off + c0) : p.guide,
+                     ok ? 16 : 0);
+        }
+      };
+
+      const int warp = tid >> 5, lane = tid & 31;
+      const int cs = warp % SM::NCS;
+      const int pbase = (warp / SM::NCS) * 32 * SM::P + lane;
+      float2 acc[SM::P][K];
+#pragma unroll
+      for (int i = 0; i < SM::P; ++i)
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc[i][k] = make_float2(0.f, 0.f);
+
+#pragma unroll
+      for (int st = 0; st < kStages - 1; ++st) {
+        if (st < nchunks) issue(st, st);
+        cp_async_commit();
+      }
+      for (int chunk = 0; chunk < nchunks; ++chunk) {
+        cp_async_wait<kStages - 2>();
+        __syncthreads();  // chunk landed for every thread; slot (chunk - 1) % kStages is free
+        if (chunk + kStages - 1 < nchunks) issue(chunk + kStages - 1, (chunk + kStages - 1) % kStages);
+        cp_async_commit();
+        const char* stage = ring + (chunk % kStages) * kStageBytes;
+#pragma unroll
+        for (int j = 0; j < SM::UPT; ++j) {
+          const int u = cs + j * SM::NCS;
+          float g[SM::P][VE];
+#pragma unroll
+          for (int i = 0; i < SM::P; ++i) {
+            const int r = pbase + 32 * i;
+            E::unpack(*reinterpret_cast<const uint4*>(stage + r * kRowBytes + ((u ^ (r & 7)) << 4)), g[i]);
+          }
+          const float* wu = s_w + (chunk * 8 + u) * K * VE;
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+#pragma unroll
+            for (int e4 = 0; e4 < VE; e4 += 4) {
+              const float4 w4 = *reinterpret_cast<const float4*>(wu + k * VE + e4);
+#pragma unroll
+              for (int i = 0; i < SM::P; ++i) {
+                acc[i][k] = __ffma2_rn(make_float2(g[i][e4], g[i][e4 + 1]), make_float2(w4.x, w4.y), acc[i][k]);
+                acc[i][k] = __ffma2_rn(make_float2(g[i][e4 + 2], g[i][e4 + 3]), make_float2(w4.z, w4.w), acc[i][k]);
+              }
+            }
+          }
+        }
+      }
+      __syncthreads();  // every warp is done reading the ring
+      float* red = reinterpret_cast<float*>(ring);  // [NCS][K][kTilePix]
+#pragma unroll
+      for (int i = 0; i < SM::P; ++i)
+#pragma unroll
+        for (int k = 0; k < K; ++k) red[(cs * K + k) * kTilePix + pbase + 32 * i] = acc[i][k].x + acc[i][k].y;
+      __syncthreads();
+    }
 
     // ------------------------------------------------------------ phase A
     {
       const int pix = tid >> 1, half = tid & 1;
       const int u = pix / CPT, t = pix - u * CPT;
-      const int unit = tile * NU + u;
-      const bool valid = unit < p.num_units;
-
       int b = 0, cy = 0, cx = 0, y = 0, x = 0;
-      if (valid) {
-        const int sub = unit % p.units_per_cell;
-        const int cell = unit / p.units_per_cell;
-        cx = cell % p.W;
-        const int rest = cell / p.W;
-        cy = rest % p.H;
-        b = rest / p.H;
-        const int ch = sub * CPT + t;
-        const int ci = ch / p.I;
-        y = cy * p.I + ci;
-        x = cx * p.I + (ch - ci * p.I);
-      }
+      const bool valid = pixel_coords<CPT>(p, tile, pix, b, cy, cx, y, x);
 
       float logit[K];
 #pragma unroll
       for (int k = 0; k < K; ++k) logit[k] = 0.f;
 
-      if (p.from_logits) {
+      if constexpr (STAGED) {
+        const float* red = reinterpret_cast<const float*>(ring);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          float a = 0.f;
+#pragma unroll
+          for (int c = 0; c < SM::NCS; ++c) a += red[(c * K + k) * kTilePix + pix];
+          logit[k] = a + s_bias[k];
+        }
+      } else if (p.from_logits) {
         if (valid && half == 0) {
           const T* lp = lbase + b * p.l_b + y * p.l_h + x * p.l_w;
 #pragma unroll
@@ -301,11 +468,13 @@ la_fwd_kernel(const __grid_constant__ Params p) {
     // ------------------------------------------------------------ phase B
     {
       const int NG = p.C / V;
+      const int g0 = (int)((int64_t)slice * NG / p.cslices);
+      const int ns = (int)((int64_t)(slice + 1) * NG / p.cslices) - g0;
       const int tile_units = min(NU, p.num_units - tile * NU);
-      const int items = tile_units * NG;
+      const int items = tile_units * ns;
       for (int it = tid; it < items; it += kThreads) {
-        const int u = it / NG;
-        const int gi = it - u * NG;
+        const int u = it / ns;
+        const int gi = g0 + (it - u * ns);
         const int unit = tile * NU + u;
         const int b = (unit / p.units_per_cell) / (p.H * p.W);
         const T* vb = vbase + b * p.v_b + gi * V;
@@ -364,6 +533,20 @@ la_fwd_kernel(const __grid_constant__ Params p) {
   }
 }
 
+// Two entry points over one body: the per-pixel variant keeps the
+// compiler's register choice (about 70, three CTAs per SM); the staged
+// variant is held to 128 registers so that two CTAs share an SM and one's
+// pooling overlaps the other's projection.
+template <typename T, int K, int CPT, bool VEC>
+__global__ void __launch_bounds__(kThreads) la_fwd_kernel(const __grid_constant__ Params p) {
+  la_fwd_body<T, K, CPT, VEC, false>(p);
+}
+
+template <typename T, int K, int CPT, bool VEC>
+__global__ void __launch_bounds__(kThreads, 2) la_fwd_staged_kernel(const __grid_constant__ Params p) {
+  la_fwd_body<T, K, CPT, VEC, true>(p);
+}
+
 // ---------------------------------------------------------------- host side
 thread_local char g_err[512] = "";
 thread_local int g_last_kernel = 0;
@@ -379,30 +562,47 @@ int fail(int code, const char* fmt, ...) {
 
 using KernelFn = void (*)(Params);
 
+// Guides at least this wide take the staged projection (measured on B200:
+// it wins once the projection is a large share of the work).
+#ifndef ULA_STAGED_MIN_CG
+#define ULA_STAGED_MIN_CG 128
+#endif
+constexpr int kStagedMinCg = ULA_STAGED_MIN_CG;
+// fp32 guides at least this wide take the tensor-core projection under AUTO.
+constexpr int kWideMinCg = 128;
+
 template <typename T, int K, int CPT>
-KernelFn pick_vec(bool vec) {
+KernelFn pick_vec(bool vec, bool staged) {
+  if (staged) return vec ? la_fwd_staged_kernel<T, K, CPT, true> : la_fwd_staged_kernel<T, K, CPT, false>;
   return vec ? la_fwd_kernel<T, K, CPT, true> : la_fwd_kernel<T, K, CPT, false>;
 }
 
 template <typename T, int K>
-KernelFn pick_cpt(int cpt, bool vec) {
-  return cpt == 4 ? pick_vec<T, K, 4>(vec) : pick_vec<T, K, 1>(vec);
+KernelFn pick_cpt(int cpt, bool vec, bool staged) {
+  return cpt == 4 ? pick_vec<T, K, 4>(vec, staged) : pick_vec<T, K, 1>(vec, staged);
 }
 
 template <typename T>
-KernelFn pick_k(int K, int cpt, bool vec) {
+KernelFn pick_k(int K, int cpt, bool vec, bool staged) {
   switch (K) {
-    case 5: return pick_cpt<T, 5>(cpt, vec);
-    case 9: return pick_cpt<T, 9>(cpt, vec);
-    case 13: return pick_cpt<T, 13>(cpt, vec);
-    case 17: return pick_cpt<T, 17>(cpt, vec);
-    case 25: return pick_cpt<T, 25>(cpt, vec);
+    case 5: return pick_cpt<T, 5>(cpt, vec, staged);
+    case 9: return pick_cpt<T, 9>(cpt, vec, staged);
+    case 13: return pick_cpt<T, 13>(cpt, vec, staged);
+    case 17: return pick_cpt<T, 17>(cpt, vec, staged);
+    case 25: return pick_cpt<T, 25>(cpt, vec, staged);
     default: return nullptr;
   }
 }
 
-size_t smem_for(int K, int cpt, int Cg, bool from_logits) {
-  auto f = [&](auto kk, auto cc) { return Smem<decltype(kk)::value, decltype(cc)::value>::bytes(Cg, from_logits); };
+// Shared memory of one CTA; `es` = element size (the staged ring holds
+// 128-byte chunks, so its weight table is padded to whole chunks).
+size_t smem_for(int K, int cpt, int Cg, bool from_logits, bool staged, int es) {
+  const int ch = kRowBytes / es;
+  const int cgp = (Cg + ch - 1) / ch * ch;
+  auto f = [&](auto kk, auto cc) {
+    using SS = Smem<decltype(kk)::value, decltype(cc)::value>;
+    return staged ? SS::staged_bytes(cgp) : SS::bytes(Cg, from_logits);
+  };
   using I1 = std::integral_constant<int, 1>;
   using I4 = std::integral_constant<int, 4>;
 #define ULA_SM(KV)                                                          \
@@ -443,14 +643,14 @@ int device_info(DevInfo* info) {
   return UPLIFT_LA_OK;
 }
 
-int launch(const Params& p0, int dtype, int K, int cpt, bool vec, size_t smem, cudaStream_t stream) {
+int launch(const Params& p0, int dtype, int K, int cpt, bool vec, bool staged, size_t smem, cudaStream_t stream) {
   Params p = p0;
   if (p.num_units == 0) return UPLIFT_LA_OK;  // empty input: nothing to do
   KernelFn fn = nullptr;
   switch (dtype) {
-    case UPLIFT_LA_F32: fn = pick_k<float>(K, cpt, vec); break;
-    case UPLIFT_LA_BF16: fn = pick_k<__nv_bfloat16>(K, cpt, vec); break;
-    case UPLIFT_LA_F16: fn = pick_k<__half>(K, cpt, vec); break;
+    case UPLIFT_LA_F32: fn = pick_k<float>(K, cpt, vec, staged); break;
+    case UPLIFT_LA_BF16: fn = pick_k<__nv_bfloat16>(K, cpt, vec, staged); break;
+    case UPLIFT_LA_F16: fn = pick_k<__half>(K, cpt, vec, staged); break;
     default: return fail(UPLIFT_LA_ERR_ARG, "unknown dtype %d", dtype);
   }
   if (fn == nullptr) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d unsupported (5, 9, 13, 17, 25)", K);
@@ -466,7 +666,17 @@ int launch(const Params& p0, int dtype, int K, int cpt, bool vec, size_t smem, c
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem);
   if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "occupancy query: %s", cudaGetErrorString(e));
   if (per_sm < 1) per_sm = 1;
-  const int grid = (int)std::min<int64_t>((int64_t)p.num_tiles, (int64_t)info.sms * per_sm);
+  const int64_t resident = (int64_t)info.sms * per_sm;
+  // Fewer tiles than resident CTAs: split each tile's channels into slices
+  // (at least 8 vectors each) unless the repeated projection would cost more
+  // than the pooling it spreads.
+  p.cslices = 1;
+  const int ng = vec ? p.C / (16 / (int)elem_size(dtype)) : p.C;
+  if (p.num_tiles < resident && (p.from_logits || p.Cg <= p.C)) {
+    const int64_t want = (resident + p.num_tiles - 1) / p.num_tiles;
+    p.cslices = (int)std::max<int64_t>(1, std::min<int64_t>(want, ng / 8));
+  }
+  const int grid = (int)std::min<int64_t>((int64_t)p.num_tiles * p.cslices, resident);
   fn<<<grid, kThreads, smem, stream>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
@@ -588,15 +798,26 @@ int uplift_la_forward(const void* guide, const int64_t guide_strides[4],
       if (rc == UPLIFT_LA_OK) g_last_kernel = UPLIFT_LA_KERNEL_TENSOR_CORE;
       return rc;
     }
+    // The wide-guide kernel (two-term bf16 split, ~1e-5 relative) pays off
+    // where the projection dominates; narrower fp32 guides keep the
+    // CUDA-core kernel's fp32 arithmetic unless the tensor cores are asked for.
+    const char* why_w = nullptr;
+    if (tcw_eligible(a, &why_w) && (policy == UPLIFT_LA_POLICY_TENSOR_CORE || Cg >= kWideMinCg)) {
+      rc = tcw_launch(a, static_cast<cudaStream_t>(stream));
+      if (rc == UPLIFT_LA_OK) g_last_kernel = UPLIFT_LA_KERNEL_TENSOR_CORE_WIDE;
+      return rc;
+    }
+    if (dtype == UPLIFT_LA_F32) why = why_w;
     if (policy == UPLIFT_LA_POLICY_TENSOR_CORE)
       return fail(UPLIFT_LA_ERR_SHAPE, "tensor-core kernel required but not applicable: %s", why);
   } else if (policy == UPLIFT_LA_POLICY_TENSOR_CORE) {
     return fail(UPLIFT_LA_ERR_SHAPE, "tensor-core kernel required but not applicable: scale I=%d != 2", I);
   }
-  const size_t smem = smem_for(K, cpt, Cg, false);
+  const bool staged = p.guide_vec && Cg >= kStagedMinCg;
+  const size_t smem = smem_for(K, cpt, Cg, false, staged, (int)elem_size(dtype));
   if (smem == 0) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d unsupported (5, 9, 13, 17, 25)", K);
-  rc = launch(p, dtype, K, cpt, vec, smem, static_cast<cudaStream_t>(stream));
-  if (rc == UPLIFT_LA_OK) g_last_kernel = UPLIFT_LA_KERNEL_SIMT;
+  rc = launch(p, dtype, K, cpt, vec, staged, smem, static_cast<cudaStream_t>(stream));
+  if (rc == UPLIFT_LA_OK) g_last_kernel = staged ? UPLIFT_LA_KERNEL_SIMT_STAGED : UPLIFT_LA_KERNEL_SIMT;
   return rc;
 }
 
@@ -619,9 +840,9 @@ int uplift_la_pool(const void* logits, const int64_t logits_strides[4],
   p.l_b = logits_strides[0]; p.l_k = logits_strides[1]; p.l_h = logits_strides[2]; p.l_w = logits_strides[3];
   p.hardmax = hardmax ? 1 : 0;
   p.from_logits = 1;
-  const size_t smem = smem_for(K, cpt, 0, true);
+  const size_t smem = smem_for(K, cpt, 0, true, false, (int)elem_size(dtype));
   if (smem == 0) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d unsupported (5, 9, 13, 17, 25)", K);
-  rc = launch(p, dtype, K, cpt, vec, smem, static_cast<cudaStream_t>(stream));
+  rc = launch(p, dtype, K, cpt, vec, false, smem, static_cast<cudaStream_t>(stream));
   if (rc == UPLIFT_LA_OK && p.num_units > 0) g_last_kernel = UPLIFT_LA_KERNEL_SIMT;
   return rc;
 }
@@ -635,7 +856,12 @@ int uplift_la_set_kernel_policy(int policy) {
 
 int uplift_la_last_kernel(void) { return ula::g_last_kernel; }
 
-int uplift_la_device_status(int clear) { return ula::tc_device_status(clear != 0); }
+int uplift_la_device_status(int clear) {
+  const int a = ula::tc_device_status(clear != 0);
+  const int b = ula::tcw_device_status(clear != 0);
+  if (a < 0 || b < 0) return -1;
+  return a != 0 ? a : b;
+}
 
 int uplift_la_test_hook(int fault, unsigned long long wait_limit_ns) {
   return ula::tc_set_test_hook(fault, wait_limit_ns);
