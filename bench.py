@@ -267,6 +267,9 @@ def run_ours(args, world, rank, local):
     # ---- whole upsampler throughput (weak scaling: 8 images per GPU)
     ups = None if args.no_upsampler else run_upsampler(dev, stream, world, rank, args)
 
+    # ---- fp32 attender configurations (standalone K=9 call, SD1.5-VAE levels)
+    fp32 = None if args.no_fp32 else run_fp32_configs(dev, stream, peak)
+
     # ---- CPU baseline (rank 0, N=1 only): reference algorithm on host cores
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -297,9 +300,66 @@ def run_ours(args, world, rank, local):
     }
     if ups is not None:
         result["upsampler"] = ups
+    if fp32 is not None:
+        result["fp32_configs"] = fp32
     if cpu is not None:
         result["cpu_baseline"] = cpu
     return result
+
+
+def run_fp32_configs(dev, stream, peak, reps=20):
+    """Device time of the fp32 attender configurations, each call replayed
+    `reps` times in a CUDA graph: the standalone call (K=9, value 384x32^2,
+    guide 64x64^2, one image; latency-bound, 8.9 MB) and the two attender
+    levels of the SD1.5-VAE upsampler (K=17, Cg=512, C=4, B=16; value 64^2
+    -> 128^2 and 128^2 -> 256^2).  Algorithmic bytes per output pixel:
+    Cg*4 + C*4 + C*4/4.  Random-init LocalAttender in fp32, N(0,1) inputs."""
+    from uplift_b200 import _native
+    from uplift_b200.attender import LocalAttender
+
+    cases = [("standalone_k9_b1_32to64", 1, 64, 384, 32, 9),
+             ("sdvae_k17_b16_64to128", 16, 512, 4, 64, 17),
+             ("sdvae_k17_b16_128to256", 16, 512, 4, 128, 17)]
+    kernel_names = {_native.KERNEL_SIMT: "la_fwd_kernel", _native.KERNEL_SIMT_STAGED: "la_fwd_staged_kernel",
+                    _native.KERNEL_TENSOR_CORE: "la_tc_kernel", _native.KERNEL_TENSOR_CORE_WIDE: "la_tcw_kernel"}
+    out = {}
+    g = torch.Generator().manual_seed(0)
+    side = torch.cuda.Stream(dev)  # graphs are captured off the default stream
+    side.wait_stream(stream)
+    stream = side
+    for name, b, cg, c, h, k in cases:
+        torch.manual_seed(0)
+        la = LocalAttender(cg, k).to(dev)
+        guide = torch.randn(b, cg, 2 * h, 2 * h, generator=g).to(dev).contiguous(memory_format=torch.channels_last)
+        value = torch.randn(b, c, h, h, generator=g).to(dev).contiguous(memory_format=torch.channels_last)
+        with torch.no_grad(), torch.cuda.stream(stream):
+            for _ in range(3):
+                la(guide, value)
+            kern = _native.last_kernel()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for _ in range(reps):
+                    la(guide, value)
+            for _ in range(5):  # warm replays (graph upload, clocks)
+                graph.replay()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            times = []
+            for _ in range(5):
+                ev[0].record(stream)
+                graph.replay()
+                ev[1].record(stream)
+                ev[1].synchronize()
+                times.append(ev[0].elapsed_time(ev[1]) / reps)
+        del graph
+        us = statistics.median(times) * 1e3
+        px = b * 4 * h * h
+        bpp = cg * 4 + c * 4 + c * 4 / 4
+        gbs = px * bpp / (us * 1e-6) / 1e9
+        out[name] = {"kernel": kernel_names.get(kern, str(kern)), "us_per_call": round(us, 2),
+                     "Mpix_s": round(px / us, 1), "GB_s": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4)}
+    out["note"] = ("fp32 storage; CUDA-graph replays of one call, median of 5; bytes = algorithmic "
+                   "(guide + output + value once); frac against the measured HBM copy peak")
+    return out
 
 
 def run_e2e(la, host, dev, stream, world, args, mpix_step):
@@ -529,6 +589,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end pass")
     ap.add_argument("--eager", action="store_true", help="time plain launches instead of a CUDA graph")
     ap.add_argument("--no-upsampler", action="store_true", help="skip the whole-upsampler img/s pass")
+    ap.add_argument("--no-fp32", action="store_true", help="skip the fp32 attender configurations")
+    ap.add_argument("--only-fp32", action="store_true",
+                    help="run only the fp32 attender configurations (profiling captures)")
     ap.add_argument("--images", type=int, default=8,
                     help="images per GPU (default 8; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -544,7 +607,11 @@ def main():
         return
     world, rank, local = dist_setup()
     try:
-        res = run_ours(args, world, rank, local)
+        if args.only_fp32:
+            dev = torch.device("cuda", local)
+            res = {"fp32_configs": run_fp32_configs(dev, torch.cuda.current_stream(dev), load_peaks()[0])}
+        else:
+            res = run_ours(args, world, rank, local)
         if rank == 0:
             print(json.dumps(res), flush=True)
     finally:

@@ -47,18 +47,30 @@ def is_stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile every .cu under uplift_b200/csrc into one shared library."""
+    """Compile every .cu under uplift_b200/csrc (one nvcc per file, in
+    parallel) and link them into one shared library."""
     if not force and not is_stale():
         return lib_path()
     LIB_DIR.mkdir(parents=True, exist_ok=True)
-    tmp = lib_path().with_suffix(".so.tmp")
-    cmd = [nvcc_path(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17",
-           "-Xcompiler", "-fPIC", "-shared", f"-I{INCLUDE}", f"-I{CSRC}",
-           "-o", str(tmp), *map(str, sources())]
+    obj_dir = LIB_DIR / "obj"
+    obj_dir.mkdir(exist_ok=True)
+    nvcc = nvcc_path()
+    common = [*ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", f"-I{CSRC}"]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd), file=sys.stderr)
-    subprocess.run(cmd, check=True)
+        common.append("-Xptxas=-v")
+    procs, objs = [], []
+    for src in sources():
+        obj = obj_dir / (src.stem + ".o")
+        cmd = [nvcc, *common, "-c", str(src), "-o", str(obj)]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        procs.append((src, subprocess.Popen(cmd)))
+        objs.append(obj)
+    failed = [src.name for src, proc in procs if proc.wait() != 0]
+    if failed:
+        raise RuntimeError(f"nvcc failed on {', '.join(failed)}")
+    tmp = lib_path().with_suffix(".so.tmp")
+    subprocess.run([nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *map(str, objs)], check=True)
     os.replace(tmp, lib_path())
     return lib_path()
 
