@@ -1,5 +1,5 @@
 """The C-ABI library builds for sm_100a, loads, and exports what
-include/uplift_la.h declares.  CPU only: argument validation runs before any
+include/*.h declare.  CPU only: argument validation runs before any
 CUDA call, so no kernel is launched here."""
 import ctypes
 import re
@@ -11,13 +11,15 @@ import torch
 from uplift_b200 import _native
 from uplift_b200.attender import LocalAttender, NEIGHBOURHOODS, neighbourhood
 
-HEADER = Path(__file__).resolve().parent.parent / "include" / "uplift_la.h"
+INCLUDE = Path(__file__).resolve().parent.parent / "include"
 
 
 def declared_functions():
-    text = HEADER.read_text()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(uplift_la_\w+)\s*\(", text)))
+    names = set()
+    for header in sorted(INCLUDE.glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(uplift_\w+)\s*\(", text))
+    return sorted(names)
 
 
 @pytest.fixture(scope="module")

@@ -29,6 +29,11 @@ EXPORTED = (
     "uplift_la_last_kernel",
     "uplift_la_device_status",
     "uplift_la_test_hook",
+    # include/uplift_glue.h
+    "uplift_resize_bilinear",
+    "uplift_resize_nearest",
+    "uplift_add_channels",
+    "uplift_bias_act",
 )
 POLICY_AUTO, POLICY_SIMT, POLICY_TENSOR_CORE = 0, 1, 2
 KERNEL_SIMT, KERNEL_TENSOR_CORE, KERNEL_SIMT_STAGED, KERNEL_TENSOR_CORE_WIDE = 1, 2, 3, 4
@@ -85,6 +90,14 @@ def load(build_if_missing: bool = False):
         lib.uplift_la_device_status.argtypes = [i]
         lib.uplift_la_test_hook.restype = i
         lib.uplift_la_test_hook.argtypes = [i, ctypes.c_ulonglong]
+        lib.uplift_resize_bilinear.restype = i
+        lib.uplift_resize_bilinear.argtypes = [vp, i64p, vp, i64p, i, i, i, i, i, i, i, i, i, vp]
+        lib.uplift_resize_nearest.restype = i
+        lib.uplift_resize_nearest.argtypes = [vp, i64p, vp, i64p, i, i, i, i, i, i, i, vp]
+        lib.uplift_add_channels.restype = i
+        lib.uplift_add_channels.argtypes = [vp, i64p, vp, i64p, i, i, i, i, i, vp]
+        lib.uplift_bias_act.restype = i
+        lib.uplift_bias_act.argtypes = [vp, i64p, vp, vp, i64p, i, i, i, i, i, i, i, vp]
         _lib = lib
     return _lib
 

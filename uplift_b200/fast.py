@@ -8,6 +8,14 @@ its Triton kernel only for K = 17 and silently keeps the PyTorch attender
 otherwise (uplift/fast.py:106-119); here every K goes to the fused sm_100a
 kernel (one launch including conv1 and the residual), and a missing library
 raises instead of falling back.
+
+The iteration loop (uplift/fast.py:168-223) runs the encoder / decoder /
+refiner convolutions as cuDNN module calls and everything between them on
+the sm_100a glue kernels (uplift_b200.glue): residual_auto adds in place
+into the fresh conv output, the up-block residual resize fused with its
+add, the skip-feature resample written straight into the concatenation
+buffer, and the final resize -- each one HBM pass, same values as the
+reference's eager ops.
 """
 from __future__ import annotations
 
@@ -18,6 +26,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import glue
+from . import uplift as U
 from .attender import AttenderWrapper, LocalAttender
 
 
@@ -58,52 +68,37 @@ class OptimizedUPLiFT(nn.Module):
         return self._forward_impl(img, x, outsize)
 
     def _forward_impl(self, img, x, outsize=None):
-        """The iteration loop of UPLiFT.forward with F.interpolate resizes
-        (as the reference's fast path, uplift/fast.py:168-223)."""
+        """The iteration loop of UPLiFT.forward (as the reference's fast path,
+        uplift/fast.py:168-223), convolutions as module calls, glue on the
+        sm_100a kernels."""
         m = self.model
         ex_feats = None
         steps = []
         for i in range(m.iters):
             if i > 0 and not m.enc_share:
                 sf = m.up_factor ** i
-                img_i = F.interpolate(img, size=(int(img.shape[2] * sf), int(img.shape[3] * sf)),
-                                      mode="bilinear", align_corners=False)
+                img_i = glue.resize_bilinear(img, (int(img.shape[2] * sf), int(img.shape[3] * sf)))
             else:
                 img_i = img
             x_in = x
             if not m.enc_share or ex_feats is None:
                 if m.patch_size == 14:
-                    img_i = F.interpolate(img_i, size=((img_i.shape[2] * 16) // 14, (img_i.shape[3] * 16) // 14),
-                                          mode="bilinear", align_corners=False)
-                enc_feats = m.encoder(img_i)
+                    img_i = glue.resize_bilinear(img_i, ((img_i.shape[2] * 16) // 14, (img_i.shape[3] * 16) // 14))
+                enc_feats = _encoder(m.encoder, img_i)
             else:
                 enc_feats = ex_feats
-            x = m.decoder(x, enc_feats)
+            x = _decoder(m.decoder, x, enc_feats)
             if m.attender is not None:
                 x = m.attender(x, x_in)
             if m.refiner is not None:
-                x = self._noise_and_combine_fast(x, enc_feats[m.ref_con], m.ref_ncat_c, m.ref_ncat_s,
-                                                 m.ref_enc_resample)
-                x = m.ref_outc(m.refiner(x))
+                x = _combine(x, enc_feats[m.ref_con], m.ref_ncat_c, m.ref_ncat_s, m.ref_enc_resample)
+                x = m.ref_outc(_group(m.refiner, x))
             ex_feats = enc_feats
             steps.append(x)
         if outsize is not None:
-            return _resize_bilinear(x, outsize)
+            return glue.resize_bilinear(x, outsize)
         if m.return_all_steps:
             return steps
-        return x
-
-    @staticmethod
-    def _noise_and_combine_fast(x, f=None, ncat_c=0, ncat_s=1, f_resample="none"):
-        if f is not None:
-            if f_resample == "nearest":
-                f = F.interpolate(f, size=(x.shape[2], x.shape[3]), mode="nearest")
-            elif f_resample == "bilinear":
-                f = F.interpolate(f, size=(x.shape[2], x.shape[3]), mode="bilinear", align_corners=False)
-            x = torch.cat([x, f], dim=1)
-        if ncat_c > 0:
-            x = torch.cat([x, ncat_s * torch.randn([x.shape[0], ncat_c, x.shape[2], x.shape[3]],
-                                                   device=x.device, dtype=x.dtype)], dim=1)
         return x
 
     def _fold_batchnorm(self):
@@ -128,19 +123,169 @@ class OptimizedUPLiFT(nn.Module):
                 del module[len(out)]
 
 
-_INT_MAX = 2**31 - 1
+# ----------------------------------------------------------------- executor
+# Module-by-module mirrors of the forward methods in uplift_b200/uplift.py
+# (the reference's uplift/uplift.py:96-531), with the glue on sm_100a
+# kernels.  A conv Sequential always returns a fresh tensor, so residual
+# sums are written into it in place.
+
+def _cl(t: torch.Tensor) -> torch.Tensor:
+    return t.contiguous(memory_format=torch.channels_last)
 
 
-def _resize_bilinear(x, size):
-    """F.interpolate(bilinear, align_corners=False), split along the batch
-    when the input or output exceeds the 2^31-element limit of torch's
-    channels_last bilinear kernel (e.g. 8 x 384 x 1168^2)."""
-    out_numel = x.shape[0] * x.shape[1] * size[0] * size[1]
-    if max(x.numel(), out_numel) <= _INT_MAX or x.shape[0] == 1:
-        return F.interpolate(x, size=size, mode="bilinear", align_corners=False)
-    per = max(1, _INT_MAX // max(x[0].numel(), out_numel // x.shape[0]))
-    return torch.cat([F.interpolate(x[i:i + per], size=size, mode="bilinear", align_corners=False)
-                      for i in range(0, x.shape[0], per)], dim=0)
+def _plain_conv(mod) -> bool:
+    return type(mod) is nn.Conv2d and mod.padding_mode == "zeros"
+
+
+# cuDNN's fused convolution + bias + ReLU (one kernel; the bias is added
+# before the single rounding of the result, where the eager conv -> + bias ->
+# ReLU rounds twice: at most one storage-type ulp apart, like the BatchNorm
+# folding of this mode)
+_CONV_RELU = getattr(torch, "cudnn_convolution_relu", None)
+
+
+def _conv_relu(mod, x):
+    if _CONV_RELU is not None and not isinstance(mod.padding, str) and x.is_cuda:
+        return _CONV_RELU(x, mod.weight, mod.bias, list(mod.stride), list(mod.padding),
+                          list(mod.dilation), mod.groups)
+    y = _cl(F.conv2d(x, mod.weight, None, mod.stride, mod.padding, mod.dilation, mod.groups))
+    return glue.bias_act_(y, mod.bias, True)
+
+
+def _conv_seq(seq, x, res=None):
+    """Run a conv Sequential (Conv [-> ReLU] ... after BatchNorm folding):
+    each Conv2d without its bias, then one epilogue pass adding the bias,
+    applying the ReLU that follows and, after the last module, adding the
+    block residual `res`.  Other modules run as they are.  Returns (y, True)
+    when `res` was added."""
+    mods = list(seq)
+    i, used = 0, False
+    while i < len(mods):
+        mod = mods[i]
+        if _plain_conv(mod):
+            relu = i + 1 < len(mods) and type(mods[i + 1]) is nn.ReLU
+            nxt = i + (2 if relu else 1)
+            r = res if nxt == len(mods) else None
+            if relu and r is None:
+                x = _conv_relu(mod, x)
+            else:
+                y = _cl(F.conv2d(x, mod.weight, None, mod.stride, mod.padding, mod.dilation, mod.groups))
+                x = glue.bias_act_(y, mod.bias, relu, r)
+            used = used or r is not None
+            i = nxt
+        else:
+            x = mod(x)
+            i += 1
+    return x, used
+
+
+def _conv_block(b, x):
+    """_ConvBlock.forward: convs (bias, ReLU and the residual_auto add fused
+    into their epilogues)."""
+    if not b.residual:
+        return _conv_seq(b.conv, x)[0]
+    xr = b.res_down(x) if b.stride == 2 else x
+    y, used = _conv_seq(b.conv, x, xr)
+    return y if used else glue.add_channels_(_cl(y), xr)
+
+
+def _transposed(mod, x):
+    """ConvTranspose2d without its bias, then the bias in one vectorised
+    pass (torch adds it with a broadcast that does not vectorise)."""
+    if type(mod) is not nn.ConvTranspose2d or mod.padding_mode != "zeros":
+        return _cl(mod(x))
+    y = F.conv_transpose2d(x, mod.weight, None, mod.stride, mod.padding, mod.output_padding, mod.groups,
+                           mod.dilation)
+    return glue.bias_act_(_cl(y), mod.bias, False)
+
+
+def _tconv(b, x):
+    """TransposeConv.forward: y = up(x) (+ bilinear x, align_corners=True)."""
+    y = _transposed(b.up, x)
+    if b.residual != "bilinear":
+        return y
+    if x.shape[1] == y.shape[1]:
+        return glue.upsample_add_(y, x, align_corners=True)
+    return glue.add_channels_(y, glue.resize_bilinear(x, y.shape[2:], align_corners=True))
+
+
+def _block(b, x):
+    if isinstance(b, U._ConvBlock):
+        return _conv_block(b, x)
+    if isinstance(b, U.TransposeConv):
+        return _tconv(b, x)
+    return b(x)
+
+
+def _group(g, x):
+    if g.count == 0:
+        return x
+    for b in g.blocks:
+        x = _block(b, x)
+    return x
+
+
+def _down(d, x):
+    if d.down is None:
+        return x
+    y = d.down(x)
+    if d.residual == "bilinear":
+        y = glue.add_channels_(_cl(y), d.res_down(x))
+    return y
+
+
+def _up(u, x):
+    """UpBlock.forward: transposed conv + bilinear (align_corners=True)
+    residual, the resize fused with the add."""
+    if u.up is None:
+        return x
+    y = _transposed(u.up, x)
+    if u.residual != "bilinear":
+        return y
+    return glue.upsample_add_(y, x, align_corners=True)
+
+
+def _combine(x, f=None, ncat_c=0, ncat_s=1, f_resample="none"):
+    """noise_and_combine: [x | resampled f | noise] written into one
+    channels_last buffer (no separate resize output, no cat pass).  The
+    noise is drawn exactly as the module path draws it."""
+    if f is None and ncat_c == 0:
+        return x
+    B, C1, H, W = x.shape
+    C2 = 0 if f is None else f.shape[1]
+    buf = torch.empty((B, C1 + C2 + ncat_c, H, W), dtype=x.dtype, device=x.device,
+                      memory_format=torch.channels_last)
+    glue.nearest_into_(buf[:, :C1], x)  # same size: a copy
+    if f is not None:
+        if f_resample == "bilinear":
+            f = glue.resize_bilinear(f, (H, W))
+        glue.nearest_into_(buf[:, C1:C1 + C2], f)
+    if ncat_c > 0:
+        noise = ncat_s * U._randn([B, ncat_c, H, W], x.device, x.dtype)
+        glue.nearest_into_(buf[:, C1 + C2:], noise)
+    return buf
+
+
+def _encoder(e, x):
+    feats = [_group(e.block_0, x)]
+    x = feats[0]
+    for i in range(1, e.down_steps + 1):
+        x = _group(getattr(e, f"block_{i}"), _down(getattr(e, f"down_{i}"), x))
+        feats.append(x)
+    return feats
+
+
+def _decoder(d, x, enc_feats):
+    x = _combine(x, enc_feats[-1], d.ncat_c, d.ncat_s, d.enc_resample)
+    x = _group(d.block_0, x)
+    for i in range(1, d.up_steps + 1):
+        x = _up(getattr(d, f"up_{i}"), x)
+        x = _combine(x, enc_feats[-1 - i], d.ncat_c, d.ncat_s, d.enc_resample)
+        x = _group(getattr(d, f"block_{i}"), x)
+    if d.using_attender:
+        return x
+    y = d.outc(x)
+    return glue.add_channels_(_cl(y), x) if d.residual_outc else y
 
 
 def _warmup(fast: OptimizedUPLiFT, image_size: int, device: torch.device):
