@@ -126,3 +126,15 @@ def test_bias_act_is_conv_epilogue(dt, cuda_lib):
                 y = F.conv2d(x, conv.weight, None, 1, 1).contiguous(memory_format=torch.channels_last)
                 got = glue.bias_act_(y, conv.bias, relu, res)
                 assert torch.equal(got, exp), (relu, c_res)
+
+
+def test_bias_act_partial_residual_vector(cuda_lib):
+    """A 3-channel residual (the image, into the encoder's first block) with
+    16-byte output vectors: the partial residual is read element-wise."""
+    dt = torch.bfloat16
+    y0 = _rand((2, 16, 33, 35), dt, seed=21)
+    img = _rand((2, 3, 33, 35), dt, seed=22)
+    bias = torch.randn(16, device=DEV).to(dt)
+    exp = residual_auto(img, y0 + bias.view(1, -1, 1, 1))
+    got = glue.bias_act_(y0.clone(), bias, False, img)
+    assert torch.equal(got, exp)

@@ -1,7 +1,8 @@
 // Resampling and residual kernels around the Local Attender in the UPLiFT
 // upsampler's fast mode (C ABI in include/uplift_glue.h).
 //
-// All three are streaming, HBM-bound NHWC kernels: a thread owns one output
+// All four are streaming, HBM-bound NHWC kernels: one CTA per output row
+// (source rows and weights uniform over the CTA), a thread owns one output
 // pixel x one 16-byte channel vector (8 bf16/fp16 or 4 fp32; one element
 // when the channel count or alignment does not allow vectors), so a warp
 // reads and writes whole contiguous channel runs.  Arithmetic in fp32 with
@@ -73,7 +74,7 @@ struct Map {
   void* dst;       int64_t d_b, d_h, d_w;
   int C, Hi, Wi, Ho, Wo;
   float scale_h, scale_w;
-  int64_t total;  // output pixels x channel vectors
+  int64_t total;  // batch size (0 for an empty problem); one CTA per output row
 };
 
 // One bilinear source coordinate (PyTorch's area_pixel_compute_source_index).
@@ -91,32 +92,34 @@ template <typename T, int VEC, bool ALIGN, bool ACC>
 __global__ void __launch_bounds__(kThreads) bilinear_kernel(const Map m) {
   const T* __restrict__ src = static_cast<const T*>(m.src);
   T* __restrict__ dst = static_cast<T*>(m.dst);
+  // one CTA per output row: the source rows and their weights are uniform
+  const int row = blockIdx.x;
+  const int oy = row % m.Ho, b = row / m.Ho;
+  int y0, yp;
+  float ly0, ly1;
+  src_coord<ALIGN>(oy, m.scale_h, m.Hi, y0, yp, ly0, ly1);
+  const T* r0 = src + b * m.s_b + y0 * m.s_h;
+  const T* r1 = r0 + yp * m.s_h;
+  T* orow = dst + b * m.d_b + oy * m.d_h;
   const int nv = m.C / VEC;
-  for (int64_t idx = (int64_t)blockIdx.x * kThreads + threadIdx.x; idx < m.total;
-       idx += (int64_t)gridDim.x * kThreads) {
-    const int v = (int)(idx % nv);
-    const int64_t pix = idx / nv;
-    const int ox = (int)(pix % m.Wo);
-    const int64_t r = pix / m.Wo;
-    const int oy = (int)(r % m.Ho);
-    const int b = (int)(r / m.Ho);
-    int y0, yp, x0, xp;
-    float ly0, ly1, lx0, lx1;
-    src_coord<ALIGN>(oy, m.scale_h, m.Hi, y0, yp, ly0, ly1);
+  const int items = m.Wo * nv;
+  for (int i = threadIdx.x; i < items; i += kThreads) {
+    const int ox = i / nv, c = (i - ox * nv) * VEC;
+    int x0, xp;
+    float lx0, lx1;
     src_coord<ALIGN>(ox, m.scale_w, m.Wi, x0, xp, lx0, lx1);
-    const T* base = src + b * m.s_b + (int64_t)v * VEC;
-    Vec<T, VEC> a, bb, c, d;
-    a.load(base + y0 * m.s_h + x0 * m.s_w);
-    bb.load(base + y0 * m.s_h + (x0 + xp) * m.s_w);
-    c.load(base + (y0 + yp) * m.s_h + x0 * m.s_w);
-    d.load(base + (y0 + yp) * m.s_h + (x0 + xp) * m.s_w);
-    T* out = dst + b * m.d_b + oy * m.d_h + ox * m.d_w + (int64_t)v * VEC;
+    Vec<T, VEC> a, bb, cc, d;
+    a.load(r0 + x0 * m.s_w + c);
+    bb.load(r0 + (x0 + xp) * m.s_w + c);
+    cc.load(r1 + x0 * m.s_w + c);
+    d.load(r1 + (x0 + xp) * m.s_w + c);
+    T* out = orow + ox * m.d_w + c;
     Vec<T, VEC> o;
     if constexpr (ACC) o.load(out);
 #pragma unroll
     for (int e = 0; e < VEC; ++e) {
       const float val = ly0 * (lx0 * St<T>::f(a.e[e]) + lx1 * St<T>::f(bb.e[e])) +
-                        ly1 * (lx0 * St<T>::f(c.e[e]) + lx1 * St<T>::f(d.e[e]));
+                        ly1 * (lx0 * St<T>::f(cc.e[e]) + lx1 * St<T>::f(d.e[e]));
       // accumulate: the resized value is rounded first, as a separate
       // resize followed by an add would round it
       o.e[e] = ACC ? St<T>::t(St<T>::f(o.e[e]) + St<T>::f(St<T>::t(val))) : St<T>::t(val);
@@ -129,20 +132,19 @@ template <typename T, int VEC>
 __global__ void __launch_bounds__(kThreads) nearest_kernel(const Map m) {
   const T* __restrict__ src = static_cast<const T*>(m.src);
   T* __restrict__ dst = static_cast<T*>(m.dst);
+  const int row = blockIdx.x;
+  const int oy = row % m.Ho, b = row / m.Ho;
+  const int sy = min((int)floorf((float)oy * m.scale_h), m.Hi - 1);
+  const T* srow = src + b * m.s_b + sy * m.s_h;
+  T* orow = dst + b * m.d_b + oy * m.d_h;
   const int nv = m.C / VEC;
-  for (int64_t idx = (int64_t)blockIdx.x * kThreads + threadIdx.x; idx < m.total;
-       idx += (int64_t)gridDim.x * kThreads) {
-    const int v = (int)(idx % nv);
-    const int64_t pix = idx / nv;
-    const int ox = (int)(pix % m.Wo);
-    const int64_t r = pix / m.Wo;
-    const int oy = (int)(r % m.Ho);
-    const int b = (int)(r / m.Ho);
-    const int sy = min((int)floorf((float)oy * m.scale_h), m.Hi - 1);
+  const int items = m.Wo * nv;
+  for (int i = threadIdx.x; i < items; i += kThreads) {
+    const int ox = i / nv, c = (i - ox * nv) * VEC;
     const int sx = min((int)floorf((float)ox * m.scale_w), m.Wi - 1);
     Vec<T, VEC> a;
-    a.load(src + b * m.s_b + sy * m.s_h + sx * m.s_w + (int64_t)v * VEC);
-    a.store(dst + b * m.d_b + oy * m.d_h + ox * m.d_w + (int64_t)v * VEC);
+    a.load(srow + sx * m.s_w + c);
+    a.store(orow + ox * m.d_w + c);
   }
 }
 
@@ -150,18 +152,17 @@ template <typename T, int VEC>
 __global__ void __launch_bounds__(kThreads) add_kernel(const Map m) {
   const T* __restrict__ src = static_cast<const T*>(m.src);
   T* __restrict__ dst = static_cast<T*>(m.dst);
+  const int row = blockIdx.x;
+  const int y = row % m.Ho, b = row / m.Ho;
+  const T* srow = src + b * m.s_b + y * m.s_h;
+  T* orow = dst + b * m.d_b + y * m.d_h;
   const int nv = m.C / VEC;
-  for (int64_t idx = (int64_t)blockIdx.x * kThreads + threadIdx.x; idx < m.total;
-       idx += (int64_t)gridDim.x * kThreads) {
-    const int v = (int)(idx % nv);
-    const int64_t pix = idx / nv;
-    const int x = (int)(pix % m.Wo);
-    const int64_t r = pix / m.Wo;
-    const int y = (int)(r % m.Ho);
-    const int b = (int)(r / m.Ho);
+  const int items = m.Wo * nv;
+  for (int i = threadIdx.x; i < items; i += kThreads) {
+    const int x = i / nv, c = (i - x * nv) * VEC;
     Vec<T, VEC> a, o;
-    a.load(src + b * m.s_b + y * m.s_h + x * m.s_w + (int64_t)v * VEC);
-    T* out = dst + b * m.d_b + y * m.d_h + x * m.d_w + (int64_t)v * VEC;
+    a.load(srow + x * m.s_w + c);
+    T* out = orow + x * m.d_w + c;
     o.load(out);
 #pragma unroll
     for (int e = 0; e < VEC; ++e) o.e[e] = St<T>::t(St<T>::f(o.e[e]) + St<T>::f(a.e[e]));
@@ -177,33 +178,34 @@ struct Epi {
   int64_t total;
 };
 
-template <typename T, int VEC, bool RELU>
+// RVEC: the residual is read with 16-byte vectors (its channel count and
+// strides allow it); otherwise element by element, only below res_c.
+template <typename T, int VEC, bool RELU, bool RVEC>
 __global__ void __launch_bounds__(kThreads) bias_act_kernel(const Epi m) {
   T* __restrict__ dst = static_cast<T*>(m.dst);
   const T* __restrict__ bias = static_cast<const T*>(m.bias);
   const T* __restrict__ res = static_cast<const T*>(m.res);
+  const int row = blockIdx.x;
+  const int y = row % m.H, b = row / m.H;
+  T* orow = dst + b * m.d_b + y * m.d_h;
+  const T* rrow = res != nullptr ? res + b * m.r_b + y * m.r_h : nullptr;
   const int nv = m.C / VEC;
-  for (int64_t idx = (int64_t)blockIdx.x * kThreads + threadIdx.x; idx < m.total;
-       idx += (int64_t)gridDim.x * kThreads) {
-    const int v = (int)(idx % nv);
-    const int64_t pix = idx / nv;
-    const int x = (int)(pix % m.W);
-    const int64_t r = pix / m.W;
-    const int y = (int)(r % m.H);
-    const int b = (int)(r / m.H);
-    const int c0 = v * VEC;
-    T* out = dst + b * m.d_b + y * m.d_h + x * m.d_w + c0;
+  const int items = m.W * nv;
+  for (int i = threadIdx.x; i < items; i += kThreads) {
+    const int x = i / nv, c0 = (i - x * nv) * VEC;
+    T* out = orow + x * m.d_w + c0;
     Vec<T, VEC> o, bv, rv;
     o.load(out);
     if (bias != nullptr) bv.load(bias + c0);
-    const bool has_res = res != nullptr && c0 < m.res_c;  // res_c is a multiple of VEC
-    if (has_res) rv.load(res + b * m.r_b + y * m.r_h + x * m.r_w + c0);
+    const bool has_res = rrow != nullptr && c0 < m.res_c;
+    const T* rp = has_res ? rrow + x * m.r_w + c0 : nullptr;
+    if (RVEC && has_res) rv.load(rp);  // res_c is a multiple of VEC
 #pragma unroll
     for (int e = 0; e < VEC; ++e) {
       float t = St<T>::f(o.e[e]);
       if (bias != nullptr) t = St<T>::f(St<T>::t(t + St<T>::f(bv.e[e])));
       if (RELU) t = fmaxf(t, 0.f);
-      if (has_res) t = t + St<T>::f(rv.e[e]);
+      if (has_res && c0 + e < m.res_c) t = t + St<T>::f(RVEC ? rv.e[e] : rp[e]);
       o.e[e] = St<T>::t(t);
     }
     o.store(out);
@@ -211,29 +213,17 @@ __global__ void __launch_bounds__(kThreads) bias_act_kernel(const Epi m) {
 }
 
 template <typename T>
-int launch_epi(const Epi& m0, bool vec, bool relu, cudaStream_t stream);
+int launch_epi(const Epi& m0, bool vec, bool rvec, bool relu, cudaStream_t stream);
 
 enum class Op { kBilinear, kNearest, kAdd };
-
-int sm_count() {
-  static int sms[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (sms[dev] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    sms[dev] = n;
-  }
-  return sms[dev];
-}
 
 template <typename T, int VEC>
 int launch_t(Op op, const Map& m0, bool align, bool acc, cudaStream_t stream) {
   Map m = m0;
-  m.total = (int64_t)(m.C / VEC) * m.Ho * m.Wo * (m.total /* batch */);
-  if (m.total == 0) return UPLIFT_LA_OK;
-  const int64_t blocks = std::min<int64_t>((m.total + kThreads - 1) / kThreads, (int64_t)sm_count() * 16);
-  const dim3 grid((unsigned)blocks);
+  const int64_t rows = (int64_t)m.Ho * m.total;  // m.total holds the batch
+  if (rows == 0 || m.Wo == 0 || m.C == 0) return UPLIFT_LA_OK;
+  if (rows >= (1ll << 31)) return fail(UPLIFT_LA_ERR_SHAPE, "glue: too many output rows");
+  const dim3 grid((unsigned)rows);
   switch (op) {
     case Op::kBilinear:
       if (align) {
@@ -267,6 +257,8 @@ int prepare(const char* what, const void* src, const int64_t* ss, const void* ds
   if (B < 0 || C < 0 || Hi < 0 || Wi < 0 || Ho < 0 || Wo < 0)
     return fail(UPLIFT_LA_ERR_SHAPE, "%s: negative size", what);
   const bool empty = (int64_t)B * C * Ho * Wo == 0;
+  if ((int64_t)C * Wo >= (1ll << 31) || (int64_t)C * Wi >= (1ll << 31))
+    return fail(UPLIFT_LA_ERR_SHAPE, "%s: a row exceeds 2^31 elements", what);
   if (!empty && (Hi == 0 || Wi == 0)) return fail(UPLIFT_LA_ERR_SHAPE, "%s: empty source", what);
   if (!empty && (src == nullptr || dst == nullptr)) return fail(UPLIFT_LA_ERR_ARG, "%s: null pointer", what);
   if ((C > 1 && ss[1] != 1) || (C > 1 && ds[1] != 1))
@@ -286,20 +278,22 @@ int prepare(const char* what, const void* src, const int64_t* ss, const void* ds
 }
 
 template <typename T>
-int launch_epi(const Epi& m0, bool vec, bool relu, cudaStream_t stream) {
+int launch_epi(const Epi& m0, bool vec, bool rvec, bool relu, cudaStream_t stream) {
   constexpr int V = 16 / sizeof(T);
   Epi m = m0;
-  const int ve = vec ? V : 1;
-  m.total = (int64_t)(m.C / ve) * m.H * m.W * m.total;
-  if (m.total == 0) return UPLIFT_LA_OK;
-  const int64_t blocks = std::min<int64_t>((m.total + kThreads - 1) / kThreads, (int64_t)sm_count() * 16);
-  const dim3 grid((unsigned)blocks);
-  if (vec) {
-    if (relu) bias_act_kernel<T, V, true><<<grid, kThreads, 0, stream>>>(m);
-    else bias_act_kernel<T, V, false><<<grid, kThreads, 0, stream>>>(m);
+  const int64_t rows = (int64_t)m.H * m.total;  // m.total holds the batch
+  if (rows == 0 || m.W == 0 || m.C == 0) return UPLIFT_LA_OK;
+  if (rows >= (1ll << 31)) return fail(UPLIFT_LA_ERR_SHAPE, "glue: too many output rows");
+  const dim3 grid((unsigned)rows);
+  if (vec && rvec) {
+    if (relu) bias_act_kernel<T, V, true, true><<<grid, kThreads, 0, stream>>>(m);
+    else bias_act_kernel<T, V, false, true><<<grid, kThreads, 0, stream>>>(m);
+  } else if (vec) {
+    if (relu) bias_act_kernel<T, V, true, false><<<grid, kThreads, 0, stream>>>(m);
+    else bias_act_kernel<T, V, false, false><<<grid, kThreads, 0, stream>>>(m);
   } else {
-    if (relu) bias_act_kernel<T, 1, true><<<grid, kThreads, 0, stream>>>(m);
-    else bias_act_kernel<T, 1, false><<<grid, kThreads, 0, stream>>>(m);
+    if (relu) bias_act_kernel<T, 1, true, false><<<grid, kThreads, 0, stream>>>(m);
+    else bias_act_kernel<T, 1, false, false><<<grid, kThreads, 0, stream>>>(m);
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "glue kernel launch: %s", cudaGetErrorString(e));
@@ -367,29 +361,39 @@ int uplift_bias_act(void* dst, const int64_t dst_strides[4], const void* bias, c
   using namespace ula::glue;
   using ula::fail;
   Map m;
-  bool vec = false;
-  const int64_t* rs = res != nullptr ? res_strides : dst_strides;
-  int rc = prepare("uplift_bias_act", res != nullptr ? res : dst, rs, dst, dst_strides, B, C, H, W, H, W, dtype,
-                   &m, &vec);
+  bool vec = false, rvec = false;
+  // output (and bias) vectors: validated with dst as its own source
+  int rc = prepare("uplift_bias_act", dst, dst_strides, dst, dst_strides, B, C, H, W, H, W, dtype, &m, &vec);
   if (rc != UPLIFT_LA_OK) return rc;
-  if (res != nullptr && (res_channels < 0 || res_channels > C))
-    return fail(UPLIFT_LA_ERR_SHAPE, "uplift_bias_act: res_channels=%d outside 0..C=%d", res_channels, C);
+  if (res != nullptr) {
+    if (res_channels < 0 || res_channels > C)
+      return fail(UPLIFT_LA_ERR_SHAPE, "uplift_bias_act: res_channels=%d outside 0..C=%d", res_channels, C);
+    if (res_strides == nullptr) return fail(UPLIFT_LA_ERR_ARG, "uplift_bias_act: null residual strides");
+    if (res_channels > 1 && res_strides[1] != 1)
+      return fail(UPLIFT_LA_ERR_LAYOUT, "uplift_bias_act: residual channel stride must be 1");
+    for (int i = 0; i < 4; ++i)
+      if (res_strides[i] < 0) return fail(UPLIFT_LA_ERR_LAYOUT, "uplift_bias_act: negative residual stride");
+  }
   const int ve = dtype == UPLIFT_LA_F32 ? 4 : 8;
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  vec = vec && (bias == nullptr || a16(bias)) && (res == nullptr || res_channels % ve == 0);
+  vec = vec && (bias == nullptr || a16(bias));
+  rvec = res != nullptr && res_channels % ve == 0 && a16(res) && res_strides[0] % ve == 0 &&
+         res_strides[2] % ve == 0 && res_strides[3] % ve == 0;
   Epi e;
   e.dst = dst; e.d_b = m.d_b; e.d_h = m.d_h; e.d_w = m.d_w;
   e.bias = bias;
   e.res = res_channels > 0 ? res : nullptr;
-  e.r_b = m.s_b; e.r_h = m.s_h; e.r_w = m.s_w;
+  e.r_b = res != nullptr ? res_strides[0] : 0;
+  e.r_h = res != nullptr ? res_strides[2] : 0;
+  e.r_w = res != nullptr ? res_strides[3] : 0;
   e.res_c = res_channels;
   e.C = C; e.H = H; e.W = W;
   e.total = m.total;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case UPLIFT_LA_F32: return launch_epi<float>(e, vec, relu != 0, s);
-    case UPLIFT_LA_BF16: return launch_epi<__nv_bfloat16>(e, vec, relu != 0, s);
-    default: return launch_epi<__half>(e, vec, relu != 0, s);
+    case UPLIFT_LA_F32: return launch_epi<float>(e, vec, rvec, relu != 0, s);
+    case UPLIFT_LA_BF16: return launch_epi<__nv_bfloat16>(e, vec, rvec, relu != 0, s);
+    default: return launch_epi<__half>(e, vec, rvec, relu != 0, s);
   }
 }
 
