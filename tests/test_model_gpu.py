@@ -94,3 +94,29 @@ def test_low_mem_equals_parallel_and_bf16_iterates(cuda_lib):
             outs.append(m(img, feats))
     assert outs[0].shape == (2, 384, 64, 64) and outs[0].dtype == torch.bfloat16
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("variant", ["dinov2-s14", "dinov3-splus16", "sd15-vae"])
+def test_fast_executor_matches_plain_all_variants(variant, cuda_lib, monkeypatch):
+    """The fast-mode executor (convs without bias + fused epilogues, glue
+    kernels, concatenation buffers, refiner and noise channels for SD1.5-VAE)
+    against the module path, fp32, same seeded noise in both, no final resize
+    (the plain path's TVF resize antialiases, the fast path's does not, as in
+    the reference)."""
+    cfg = get_config(variant)
+    torch.manual_seed(0)
+    m = U.UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift).eval().to(DEV)
+    m.enable_iterative(2)
+    g = torch.Generator().manual_seed(5)
+    side = 64 if variant == "sd15-vae" else 112
+    lat = side // cfg.backbone.patch
+    img = torch.rand(2, 3, side, side, generator=g).to(DEV)
+    feats = torch.randn(2, cfg.backbone.channel, lat, lat, generator=g).to(DEV)
+    fast = make_fast(m, compile=False, device=torch.device(DEV))
+    monkeypatch.setattr(U, "_randn", SeededNoise(77))
+    with torch.no_grad():
+        y_plain = m(img, feats)
+    monkeypatch.setattr(U, "_randn", SeededNoise(77))
+    y_fast = fast(img, feats)
+    assert y_fast.shape == y_plain.shape
+    assert normwise_err(y_fast, y_plain) <= 1e-4, normwise_err(y_fast, y_plain)
