@@ -490,7 +490,8 @@ def run_upsampler(dev, stream, world, rank, args, img_px=1022, feat_px=73, iters
             "scaling": "strong (global batch fixed, sharded over ranks)", "steps": steps,
             "config": f"UPLiFT DINOv2-S/14-shaped, random init, bf16, images {img_px}^2, feats 384x{feat_px}^2, "
                       f"iters={iters}, outsize={img_px}; make_fast(compile=False): BatchNorm folded, "
-                      f"channels_last, cuDNN convs (benchmark mode), attender fused kernel"}
+                      f"channels_last, cuDNN convs (benchmark mode; fused conv+ReLU), conv epilogues, resampling and "
+                      f"concatenation on the glue kernels, attender fused kernel"}
 
 
 def cpu_sample_inputs(host, seed=1):
