@@ -593,6 +593,8 @@ def main():
     ap.add_argument("--no-fp32", action="store_true", help="skip the fp32 attender configurations")
     ap.add_argument("--only-fp32", action="store_true",
                     help="run only the fp32 attender configurations (profiling captures)")
+    ap.add_argument("--only-upsampler", action="store_true",
+                    help="run only the whole-upsampler pass (profiling captures)")
     ap.add_argument("--images", type=int, default=8,
                     help="images per GPU (default 8; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -611,6 +613,9 @@ def main():
         if args.only_fp32:
             dev = torch.device("cuda", local)
             res = {"fp32_configs": run_fp32_configs(dev, torch.cuda.current_stream(dev), load_peaks()[0])}
+        elif args.only_upsampler:
+            dev = torch.device("cuda", local)
+            res = {"upsampler": run_upsampler(dev, torch.cuda.current_stream(dev), world, rank, args)}
         else:
             res = run_ours(args, world, rank, local)
         if rank == 0:
