@@ -247,7 +247,9 @@ def noise_and_combine(x, f=None, ncat_c=0, ncat_s=1, f_resample="none"):
     Gaussian noise channels scaled by `ncat_s` (uplift/uplift.py:354-367)."""
     if f is not None:
         if f_resample == "nearest":
-            f = TVF.resize(f, [x.shape[2], x.shape[3]], interpolation=transforms.InterpolationMode.NEAREST)
+            # TVF.resize(NEAREST) == F.interpolate(mode="nearest") value for
+            # value; this skips its fp32 round trip for bf16 / fp16 maps
+            f = F.interpolate(f, size=(x.shape[2], x.shape[3]), mode="nearest")
         elif f_resample == "bilinear":
             f = TVF.resize(f, [x.shape[2], x.shape[3]], interpolation=transforms.InterpolationMode.BILINEAR)
         x = torch.cat([x, f], dim=1)
