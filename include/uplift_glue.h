@@ -25,6 +25,10 @@
  *                           (the folded Conv -> BatchNorm -> ReLU and the
  *                           1x1 conv + residual_auto of _ConvBlock,
  *                           uplift/uplift.py:96-217), in place, in one pass
+ *   uplift_layernorm_act    Conv (bias) -> LayerNorm over channels
+ *                           ("channels_first", uplift/uplift.py:50-92) ->
+ *                           ReLU of the SD1.5-VAE variant's blocks, in place,
+ *                           one pass (per-pixel mean and variance over C)
  *
  * Tensors: base pointer + element strides in the order [B, channel, row,
  * col]; the channel stride must be 1 (channels_last / NHWC), other strides
@@ -76,6 +80,15 @@ int uplift_add_channels(void* dst, const int64_t dst_strides[4],
 int uplift_bias_act(void* dst, const int64_t dst_strides[4], const void* bias,
                     const void* res, const int64_t res_strides[4], int res_channels,
                     int relu, int B, int C, int H, int W, int dtype, void* stream);
+
+/* In place over dst[B, C, H, W], per pixel: t = dst + pre_bias[c] (when
+ * given), mu = mean_c t, var = mean_c (t - mu)^2,
+ * out = weight[c] * (t - mu) / sqrt(var + eps) + bias[c], max(out, 0) when
+ * relu.  pre_bias, weight, bias: [C] in the storage type (weight and bias
+ * required).  fp32 arithmetic, one rounding of the result. */
+int uplift_layernorm_act(void* dst, const int64_t dst_strides[4], const void* pre_bias,
+                         const void* weight, const void* bias, float eps, int relu,
+                         int B, int C, int H, int W, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -138,3 +138,33 @@ def test_bias_act_partial_residual_vector(cuda_lib):
     exp = residual_auto(img, y0 + bias.view(1, -1, 1, 1))
     got = glue.bias_act_(y0.clone(), bias, False, img)
     assert torch.equal(got, exp)
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_layernorm_act_matches_module(dt, cuda_lib):
+    """Conv (no bias) + fused bias / channels-first LayerNorm / ReLU against
+    the eager Conv -> LayerNorm -> ReLU of the SD1.5-VAE blocks."""
+    from uplift_b200.uplift import LayerNorm
+    for cin, c in ((16, 512), (8, 64), (12, 24), (4, 3)):  # vector paths of several widths, scalar path
+        conv = torch.nn.Conv2d(cin, c, 3, padding=1).to(DEV).to(dt).to(memory_format=torch.channels_last)
+        ln = LayerNorm(c, eps=1e-6, data_format="channels_first").to(DEV).to(dt)
+        with torch.no_grad():
+            ln.weight.normal_()
+            ln.bias.normal_()
+            x = _rand((2, cin, 9, 13), dt, seed=c)
+            for relu in (False, True):
+                # reference: the same LayerNorm in fp32 on the rounded conv
+                # output (eager fp16 / bf16 would round every intermediate;
+                # the kernel computes in fp32 and rounds once)
+                t = conv(x).float()
+                mu = t.mean(1, keepdim=True)
+                var = (t - mu).pow(2).mean(1, keepdim=True)
+                exp = ln.weight.float()[:, None, None] * ((t - mu) / torch.sqrt(var + ln.eps)) \
+                    + ln.bias.float()[:, None, None]
+                if relu:
+                    exp = torch.relu(exp)
+                y = F.conv2d(x, conv.weight, None, 1, 1).contiguous(memory_format=torch.channels_last)
+                got = glue.layernorm_act_(y, conv.bias, ln.weight, ln.bias, ln.eps, relu)
+                tol = {torch.float32: 1e-5, torch.bfloat16: 2 ** -8, torch.float16: 2 ** -11}[dt]
+                err = ((got.float() - exp).abs() / exp.abs().clamp_min(1.0)).max().item()
+                assert err <= tol, (cin, c, relu, err)

@@ -34,6 +34,7 @@ EXPORTED = (
     "uplift_resize_nearest",
     "uplift_add_channels",
     "uplift_bias_act",
+    "uplift_layernorm_act",
 )
 POLICY_AUTO, POLICY_SIMT, POLICY_TENSOR_CORE = 0, 1, 2
 KERNEL_SIMT, KERNEL_TENSOR_CORE, KERNEL_SIMT_STAGED, KERNEL_TENSOR_CORE_WIDE = 1, 2, 3, 4
@@ -98,6 +99,8 @@ def load(build_if_missing: bool = False):
         lib.uplift_add_channels.argtypes = [vp, i64p, vp, i64p, i, i, i, i, i, vp]
         lib.uplift_bias_act.restype = i
         lib.uplift_bias_act.argtypes = [vp, i64p, vp, vp, i64p, i, i, i, i, i, i, i, vp]
+        lib.uplift_layernorm_act.restype = i
+        lib.uplift_layernorm_act.argtypes = [vp, i64p, vp, vp, vp, ctypes.c_float, i, i, i, i, i, i, vp]
         _lib = lib
     return _lib
 

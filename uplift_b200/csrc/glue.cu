@@ -1,7 +1,7 @@
 // Resampling and residual kernels around the Local Attender in the UPLiFT
 // upsampler's fast mode (C ABI in include/uplift_glue.h).
 //
-// All four are streaming, HBM-bound NHWC kernels: one CTA per output row
+// All are streaming, HBM-bound NHWC kernels: one CTA per output row
 // (source rows and weights uniform over the CTA), a thread owns one output
 // pixel x one 16-byte channel vector (8 bf16/fp16 or 4 fp32; one element
 // when the channel count or alignment does not allow vectors), so a warp
@@ -215,6 +215,131 @@ __global__ void __launch_bounds__(kThreads) bias_act_kernel(const Epi m) {
 template <typename T>
 int launch_epi(const Epi& m0, bool vec, bool rvec, bool relu, cudaStream_t stream);
 
+// LayerNorm over the channels of each pixel (+ optional conv bias before,
+// ReLU after): one warp per pixel with the pixel's C values in registers
+// (VPL vectors of VEC per lane); the per-channel bias and affine terms are
+// staged once per CTA in shared memory (fp32, [3][C]).
+struct Ln {
+  void* dst; int64_t d_b, d_h, d_w;
+  const void* pre_bias;
+  const void* weight;
+  const void* bias;
+  float eps;
+  int C, H, W;
+  int64_t pixels;
+};
+
+constexpr int kLnWarps = 8;  // warps per CTA
+
+template <typename T, int VEC, int VPL, bool RELU>
+__global__ void __launch_bounds__(kLnWarps * 32) layernorm_kernel(const Ln a) {
+  extern __shared__ float ln_smem[];
+  T* __restrict__ dst = static_cast<T*>(a.dst);
+  const T* __restrict__ pb = static_cast<const T*>(a.pre_bias);
+  const T* __restrict__ wt = static_cast<const T*>(a.weight);
+  const T* __restrict__ bs = static_cast<const T*>(a.bias);
+  float* s_w = ln_smem;
+  float* s_b = ln_smem + a.C;
+  float* s_p = ln_smem + 2 * a.C;
+  for (int c = threadIdx.x; c < a.C; c += kLnWarps * 32) {
+    s_w[c] = St<T>::f(wt[c]);
+    s_b[c] = St<T>::f(bs[c]);
+    s_p[c] = pb != nullptr ? St<T>::f(pb[c]) : 0.f;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int nvec = a.C / VEC;
+  const bool has_pb = pb != nullptr;
+  const float inv_c = 1.f / (float)a.C;
+  const int64_t wstride = (int64_t)gridDim.x * kLnWarps;
+  for (int64_t pix = (int64_t)blockIdx.x * kLnWarps + (threadIdx.x >> 5); pix < a.pixels; pix += wstride) {
+    const int x = (int)(pix % a.W);
+    const int64_t r = pix / a.W;
+    const int y = (int)(r % a.H);
+    const int bb = (int)(r / a.H);
+    T* row = dst + bb * a.d_b + y * a.d_h + x * a.d_w;
+    float t[VPL][VEC];
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int v = lane + 32 * j;
+      Vec<T, VEC> xv;
+      if (v < nvec) xv.load(row + v * VEC);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        float q = 0.f;
+        if (v < nvec) {
+          q = St<T>::f(xv.e[e]);
+          // the conv output plus its bias, rounded as the eager add would
+          if (has_pb) q = St<T>::f(St<T>::t(q + s_p[v * VEC + e]));
+        }
+        t[j][e] = q;
+        sum += q;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mu = sum * inv_c;
+    float sq = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int v = lane + 32 * j;
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const float d = t[j][e] - mu;
+        sq += v < nvec ? d * d : 0.f;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float den = sqrtf(sq * inv_c + a.eps);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int v = lane + 32 * j;
+      if (v >= nvec) continue;
+      Vec<T, VEC> ov;
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const int c = v * VEC + e;
+        float o = s_w[c] * ((t[j][e] - mu) / den) + s_b[c];
+        if (RELU) o = fmaxf(o, 0.f);
+        ov.e[e] = St<T>::t(o);
+      }
+      ov.store(row + v * VEC);
+    }
+  }
+}
+
+template <typename T, int VEC>
+int launch_ln_v(const Ln& a, int vpl, bool relu, cudaStream_t stream) {
+  const int64_t blocks64 = std::min<int64_t>((a.pixels + kLnWarps - 1) / kLnWarps, 148ll * 32);
+  const dim3 grid((unsigned)blocks64), block(kLnWarps * 32);
+  const size_t smem = 3 * sizeof(float) * (size_t)a.C;
+#define ULA_LN(V)                                                                           \
+  case V:                                                                                   \
+    if (relu) layernorm_kernel<T, VEC, V, true><<<grid, block, smem, stream>>>(a);          \
+    else layernorm_kernel<T, VEC, V, false><<<grid, block, smem, stream>>>(a);              \
+    break;
+  switch (vpl) {
+    ULA_LN(1) ULA_LN(2) ULA_LN(4) ULA_LN(8) ULA_LN(16)
+    default: return fail(UPLIFT_LA_ERR_SHAPE, "uplift_layernorm_act: too many channels");
+  }
+#undef ULA_LN
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "glue kernel launch: %s", cudaGetErrorString(e));
+  return UPLIFT_LA_OK;
+}
+
+template <typename T>
+int launch_ln(const Ln& a, bool vec, bool relu, cudaStream_t stream) {
+  constexpr int V = 16 / sizeof(T);
+  const int ve = vec ? V : 1;
+  const int nvec = a.C / ve;
+  int vpl = 1;
+  while (vpl * 32 < nvec) vpl *= 2;
+  return vec ? launch_ln_v<T, V>(a, vpl, relu, stream) : launch_ln_v<T, 1>(a, vpl, relu, stream);
+}
+
 enum class Op { kBilinear, kNearest, kAdd };
 
 template <typename T, int VEC>
@@ -394,6 +519,33 @@ int uplift_bias_act(void* dst, const int64_t dst_strides[4], const void* bias, c
     case UPLIFT_LA_F32: return launch_epi<float>(e, vec, rvec, relu != 0, s);
     case UPLIFT_LA_BF16: return launch_epi<__nv_bfloat16>(e, vec, rvec, relu != 0, s);
     default: return launch_epi<__half>(e, vec, rvec, relu != 0, s);
+  }
+}
+
+int uplift_layernorm_act(void* dst, const int64_t dst_strides[4], const void* pre_bias, const void* weight,
+                         const void* bias, float eps, int relu, int B, int C, int H, int W, int dtype, void* stream) {
+  using namespace ula::glue;
+  using ula::fail;
+  Map m;
+  bool vec = false;
+  int rc = prepare("uplift_layernorm_act", dst, dst_strides, dst, dst_strides, B, C, H, W, H, W, dtype, &m, &vec);
+  if (rc != UPLIFT_LA_OK) return rc;
+  if (m.total > 0 && (weight == nullptr || bias == nullptr))
+    return fail(UPLIFT_LA_ERR_ARG, "uplift_layernorm_act: null weight / bias");
+  const int ve = dtype == UPLIFT_LA_F32 ? 4 : 8;
+  if (C > 16 * 32 * (vec ? ve : 1) || C > 4096)
+    return fail(UPLIFT_LA_ERR_SHAPE, "uplift_layernorm_act: C=%d above the register-resident limit", C);
+  Ln a;
+  a.dst = dst; a.d_b = m.d_b; a.d_h = m.d_h; a.d_w = m.d_w;
+  a.pre_bias = pre_bias; a.weight = weight; a.bias = bias; a.eps = eps;
+  a.C = C; a.H = H; a.W = W;
+  a.pixels = (int64_t)m.total * H * W;
+  if (a.pixels == 0 || C == 0) return UPLIFT_LA_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case UPLIFT_LA_F32: return launch_ln<float>(a, vec, relu != 0, s);
+    case UPLIFT_LA_BF16: return launch_ln<__nv_bfloat16>(a, vec, relu != 0, s);
+    default: return launch_ln<__half>(a, vec, relu != 0, s);
   }
 }
 

@@ -162,7 +162,19 @@ def _conv_seq(seq, x, res=None):
     i, used = 0, False
     while i < len(mods):
         mod = mods[i]
-        if _plain_conv(mod):
+        if (_plain_conv(mod) and i + 1 < len(mods) and type(mods[i + 1]) is U.LayerNorm
+                and mods[i + 1].data_format == "channels_first"):
+            # Conv -> LayerNorm over channels [-> ReLU]: one pass after the conv
+            ln = mods[i + 1]
+            relu = i + 2 < len(mods) and type(mods[i + 2]) is nn.ReLU
+            nxt = i + (3 if relu else 2)
+            y = _cl(F.conv2d(x, mod.weight, None, mod.stride, mod.padding, mod.dilation, mod.groups))
+            x = glue.layernorm_act_(y, mod.bias, ln.weight, ln.bias, ln.eps, relu)
+            if res is not None and nxt == len(mods):
+                x = glue.add_channels_(x, res)
+                used = True
+            i = nxt
+        elif _plain_conv(mod):
             relu = i + 1 < len(mods) and type(mods[i + 1]) is nn.ReLU
             nxt = i + (2 if relu else 1)
             r = res if nxt == len(mods) else None

@@ -127,6 +127,35 @@ def bias_act_raw_(y: torch.Tensor, bias: torch.Tensor | None, relu: bool,
     return y
 
 
+def _param(t: torch.Tensor | None, like: torch.Tensor, C: int, what: str):
+    if t is None:
+        return None
+    t = t.detach()
+    if t.dtype != like.dtype or not t.is_contiguous() or t.device != like.device:
+        t = t.to(device=like.device, dtype=like.dtype).contiguous()
+    if t.numel() != C:
+        raise ValueError(f"{what} has {t.numel()} entries for {C} channels")
+    return t
+
+
+def layernorm_act_raw_(y: torch.Tensor, pre_bias: torch.Tensor | None, weight: torch.Tensor,
+                       bias: torch.Tensor, eps: float, relu: bool) -> torch.Tensor:
+    """In place: y = relu?(LayerNorm_c(y + pre_bias) * weight + bias), the
+    "channels_first" LayerNorm of uplift/uplift.py:50-92 following a conv run
+    without its bias (the SD1.5-VAE blocks: Conv -> LayerNorm -> ReLU)."""
+    dev = _check(y)
+    B, C, H, W = y.shape
+    pb = _param(pre_bias, y, C, "pre_bias")
+    w = _param(weight, y, C, "weight")
+    b = _param(bias, y, C, "bias")
+    with torch.cuda.device(dev):
+        rc = _native.load().uplift_layernorm_act(
+            y.data_ptr(), _native.strides(y), None if pb is None else pb.data_ptr(), w.data_ptr(), b.data_ptr(),
+            float(eps), int(bool(relu)), B, C, H, W, _DTYPES[y.dtype], _stream(dev))
+    _native.check(rc, "uplift_layernorm_act")
+    return y
+
+
 # ----------------------------------------------------------------- custom ops
 @torch.library.custom_op("uplift_b200::resize_bilinear", mutates_args=())
 def _resize_bilinear_op(x: torch.Tensor, size: list[int], align_corners: bool) -> torch.Tensor:
@@ -156,6 +185,18 @@ def _add_channels_op(dst: torch.Tensor, src: torch.Tensor) -> None:
 @torch.library.custom_op("uplift_b200::bias_act_", mutates_args=("y",))
 def _bias_act_op(y: torch.Tensor, bias: Optional[torch.Tensor], relu: bool, res: Optional[torch.Tensor]) -> None:
     bias_act_raw_(y, bias, relu, res)
+
+
+@torch.library.custom_op("uplift_b200::layernorm_act_", mutates_args=("y",))
+def _layernorm_act_op(y: torch.Tensor, pre_bias: Optional[torch.Tensor], weight: torch.Tensor, bias: torch.Tensor,
+                      eps: float, relu: bool) -> None:
+    layernorm_act_raw_(y, pre_bias, weight, bias, eps, relu)
+
+
+def layernorm_act_(y, pre_bias, weight, bias, eps, relu=False):
+    """y = relu?(LayerNorm over channels of (y + pre_bias)), in place."""
+    torch.ops.uplift_b200.layernorm_act_(y, pre_bias, weight, bias, float(eps), bool(relu))
+    return y
 
 
 def bias_act_(y, bias, relu=False, res=None):
