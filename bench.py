@@ -265,7 +265,8 @@ def run_ours(args, world, rank, local):
     e2e = None if args.no_e2e else run_e2e(la, host, dev, stream, world, args, mpix_step)
 
     # ---- whole upsampler throughput (weak scaling: 8 images per GPU)
-    ups = None if args.no_upsampler else run_upsampler(dev, stream, world, rank, args)
+    ups = None if args.no_upsampler else run_upsampler(dev, stream, world, rank, args, outsize=1022)
+    models = None if args.no_upsampler else run_model_configs(dev, stream, world, rank, args)
 
     # ---- fp32 attender configurations (standalone K=9 call, SD1.5-VAE levels)
     fp32 = None if args.no_fp32 else run_fp32_configs(dev, stream, peak)
@@ -300,6 +301,8 @@ def run_ours(args, world, rank, local):
     }
     if ups is not None:
         result["upsampler"] = ups
+    if models is not None:
+        result["upsampler_other_configs"] = models
     if fp32 is not None:
         result["fp32_configs"] = fp32
     if cpu is not None:
@@ -432,22 +435,24 @@ def run_e2e(la, host, dev, stream, world, args, mpix_step):
             "pipelining": "H2D of step i+1 and D2H of step i-1 overlap step i's compute (3 streams, 2 slots)"}
 
 
-def run_upsampler(dev, stream, world, rank, args, img_px=1022, feat_px=73, iters=4, global_images=64,
-                  micro_batch=8):
-    """Whole-upsampler throughput, batch-sharded: the DINOv2-S/14-shaped UPLiFT
-    (random init, bf16, eval, channels_last) on images img_px^2 with features
-    384 x feat_px^2, iters=4, outsize=img_px; a global batch of
-    `global_images` split into contiguous shards, one per rank, each run in
-    micro-batches of `micro_batch` images.  Encoder/decoder convs are cuDNN,
-    the attender is the fused kernel.  Inputs are resident on the device
-    (synthetic, seed 0); img/s = global images / max-over-ranks time."""
+def run_upsampler(dev, stream, world, rank, args, variant="dinov2-s14", img_px=1022, feat_px=73, iters=4,
+                  global_images=64, micro_batch=8, dtype=torch.bfloat16, outsize=None, img_range=(0.0, 1.0)):
+    """Whole-upsampler throughput, batch-sharded: the `variant`-shaped UPLiFT
+    (random init, eval, channels_last) on images img_px^2 in `img_range`
+    with backbone features C x feat_px^2 (N(0,1)), iters, final resize to
+    `outsize` (None: none); a global batch of `global_images` split into
+    contiguous shards, one per rank, each run in micro-batches of
+    `micro_batch` images.  Convolutions are cuDNN, the glue between them and
+    the attender are this package's kernels.  Inputs are resident on the
+    device (synthetic, seed 1000 + rank); img/s = global images /
+    max-over-ranks time."""
     from uplift_b200.configs import get_config
     from uplift_b200.sharding import shard_bounds
     from uplift_b200.uplift import UPLiFT
     from uplift_b200.fast import make_fast
-    cfg = get_config("dinov2-s14")
+    cfg = get_config(variant)
     torch.manual_seed(0)
-    model = UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift, dtype=torch.bfloat16).eval()
+    model = UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift, dtype=dtype).eval()
     model.enable_iterative(iters)
     # the reference's fast-mode recipe for the convolutions (BatchNorm folded,
     # channels_last), without torch.compile; cuDNN picks its algorithms
@@ -457,16 +462,18 @@ def run_upsampler(dev, stream, world, rank, args, img_px=1022, feat_px=73, iters
     g = torch.Generator().manual_seed(1000 + rank)
     mine = hi - lo
     mb = min(micro_batch, max(mine, 1))
-    img = torch.rand(mb, 3, img_px, img_px, generator=g).to(torch.bfloat16).to(dev)
-    feats = torch.randn(mb, 384, feat_px, feat_px, generator=g).to(torch.bfloat16).to(dev)
+    a, b = img_range
+    img = (torch.rand(mb, 3, img_px, img_px, generator=g) * (b - a) + a).to(dtype).to(dev)
+    feats = torch.randn(mb, cfg.backbone.channel, feat_px, feat_px, generator=g).to(dtype).to(dev)
     img = img.contiguous(memory_format=torch.channels_last)
     feats = feats.contiguous(memory_format=torch.channels_last)
+    size = None if outsize is None else [outsize, outsize]
 
     def one_pass():
-        done = 0
+        done, out = 0, None
         while done < mine:
             n = min(mb, mine - done)
-            out = fast(img[:n], feats[:n], [img_px, img_px])
+            out = fast(img[:n], feats[:n], size)
             done += n
         return out
 
@@ -484,14 +491,36 @@ def run_upsampler(dev, stream, world, rank, args, img_px=1022, feat_px=73, iters
         torch.cuda.synchronize(dev)
         barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
-    assert out.shape[1:] == (384, img_px, img_px)
+    if out is not None:
+        assert out.shape[1] == cfg.backbone.channel
+    del fast, model, img, feats, out
+    torch.cuda.empty_cache()
+    dt = {torch.bfloat16: "bf16", torch.float32: "fp32"}[dtype]
+    shape = f"{outsize}^2 output" if outsize else "no final resize"
     return {"img_per_s": round(global_images / (ms / 1e3), 2), "ms_per_global_batch": round(ms, 2),
             "global_images": global_images, "images_per_gpu": mine, "micro_batch": mb,
             "scaling": "strong (global batch fixed, sharded over ranks)", "steps": steps,
-            "config": f"UPLiFT DINOv2-S/14-shaped, random init, bf16, images {img_px}^2, feats 384x{feat_px}^2, "
-                      f"iters={iters}, outsize={img_px}; make_fast(compile=False): BatchNorm folded, "
-                      f"channels_last, cuDNN convs (benchmark mode; fused conv+ReLU), conv epilogues, resampling and "
-                      f"concatenation on the glue kernels, attender fused kernel"}
+            "config": f"UPLiFT {variant}-shaped, random init, {dt}, images {img_px}^2 in {list(img_range)}, "
+                      f"feats {cfg.backbone.channel}x{feat_px}^2, iters={iters}, {shape}; make_fast(compile=False): "
+                      f"BatchNorm folded, channels_last, cuDNN convs (benchmark mode; fused conv+ReLU), conv "
+                      f"epilogues, LayerNorm, resampling and concatenation on the glue kernels, attender fused "
+                      f"kernel"}
+
+
+def run_model_configs(dev, stream, world, rank, args):
+    """The other two model configurations, whole upsampler, batch-sharded:
+    DINOv3-S+/16 at 512 px (features 384 x 32^2, iters=4, outsize 512,
+    bf16, global batch 32; low_mem=True runs the same fused kernel, so one
+    line covers both settings) and SD1.5-VAE at 512 px (latent 4 x 64^2,
+    iters=2 -> 256^2, fp32, global batch 16)."""
+    return {
+        "dinov3_splus16_512_b32_bf16": run_upsampler(
+            dev, stream, world, rank, args, variant="dinov3-splus16", img_px=512, feat_px=32, iters=4,
+            global_images=32, micro_batch=16, dtype=torch.bfloat16, outsize=512),
+        "sd15_vae_512_b16_fp32": run_upsampler(
+            dev, stream, world, rank, args, variant="sd15-vae", img_px=512, feat_px=64, iters=2,
+            global_images=16, micro_batch=8, dtype=torch.float32, outsize=None, img_range=(-1.0, 1.0)),
+    }
 
 
 def cpu_sample_inputs(host, seed=1):
@@ -615,7 +644,7 @@ def main():
             res = {"fp32_configs": run_fp32_configs(dev, torch.cuda.current_stream(dev), load_peaks()[0])}
         elif args.only_upsampler:
             dev = torch.device("cuda", local)
-            res = {"upsampler": run_upsampler(dev, torch.cuda.current_stream(dev), world, rank, args)}
+            res = {"upsampler": run_upsampler(dev, torch.cuda.current_stream(dev), world, rank, args, outsize=1022)}
         else:
             res = run_ours(args, world, rank, local)
         if rank == 0:
