@@ -290,7 +290,12 @@ def run_ours(args, world, rank, local):
                    "parallelism": f"batch-sharded x{world}, no data-path collective"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": traffic, "algo_bytes_per_step": algo_bytes_step,
+                     # every launch of a step is the attender kernel: achieved = mean launch's
+                     # algorithmic bytes / mean launch duration; traffic = the mean launch's
+                     # ncu DRAM bytes (read + write) against its algorithmic bytes
+                     "traffic": None if traffic is None else round(traffic / len(LEVELS)),
+                     "algo_bytes_per_launch": round(algo_bytes_step / len(LEVELS)),
+                     "traffic_per_step": traffic, "algo_bytes_per_step": algo_bytes_step,
                      "algo_bytes_per_pixel": bpp,
                      "kernel_ms_per_level_eager": [round(x / args.steps, 4) for x in kern_ms],
                      "gbs_per_level_eager": lvl_gbs,
