@@ -96,6 +96,31 @@ int uplift_la_pool(const void* logits, const int64_t logits_strides[4],
                    const int8_t* offsets, int pn,
                    int dtype, int hardmax, void* stream);
 
+/*
+ * Backward of uplift_la_forward (training; replaces autograd through the
+ * reference's LocalAttender.forward, uplift/uplift.py:801-847, as used by
+ * uplift/train_uplift.py).  Given dout [B, C, I*H, I*W] (strides ds), writes
+ * dguide [B, Cg, I*H, I*W] and dvalue [B, C, H, W] (storage type; either may
+ * be NULL) and ADDS the projection gradients into dweight [K, Cg] and dbias
+ * [K] (fp32, caller-zeroed; either may be NULL).  `probs` is a caller-
+ * provided fp32 workspace of B*(I*H)*(I*W)*K floats that receives the
+ * softmax weights (recomputed from the guide).  Other arguments as for
+ * uplift_la_forward; all tensors channel stride 1.  fp32 arithmetic; three
+ * kernel launches on `stream`; dweight / dbias accumulate with atomic adds,
+ * so their last bits depend on the launch schedule.
+ */
+int uplift_la_backward(const void* dout, const int64_t dout_strides[4],
+                       const void* guide, const int64_t guide_strides[4],
+                       const void* value, const int64_t value_strides[4],
+                       const float* weight, const float* bias,
+                       float* probs,
+                       void* dguide, const int64_t dguide_strides[4],
+                       void* dvalue, const int64_t dvalue_strides[4],
+                       float* dweight, float* dbias,
+                       int B, int Cg, int C, int H, int W, int I, int K,
+                       const int8_t* offsets, int pn, int conv_res, int dtype, int hardmax,
+                       void* stream);
+
 /* Kernel selection for uplift_la_forward (process-wide; default AUTO).
  * AUTO picks a tensor-core kernel (tcgen05 MMA, TMEM accumulators, TMA)
  * when one applies -- bf16/fp16 storage, I = 2, Cg = 64, C a multiple of 64

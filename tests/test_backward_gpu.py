@@ -1,0 +1,97 @@
+"""Backward of the fused Local Attender (uplift_la_backward through the
+`uplift_b200::local_attender` custom op's autograd) against fp64 autograd
+through the oracle, which restates the reference's differentiable module
+(uplift/uplift.py:801-847)."""
+import pytest
+import torch
+
+from conftest import normwise_err
+from oracle import local_attender_oracle as lao
+from uplift_b200 import ops
+from uplift_b200.attender import LocalAttender, neighbourhood
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _case(K, I, B, Cg, C, H, W, seed, dt=torch.float32, wscale=0.3):
+    g = torch.Generator().manual_seed(seed)
+    guide = torch.randn(B, Cg, I * H, I * W, generator=g).to(dt)
+    value = torch.randn(B, C, H, W, generator=g).to(dt)
+    weight = (torch.randn(K, Cg, generator=g) * wscale).to(dt)
+    bias = (torch.randn(K, generator=g) * 0.5).to(dt)
+    gout = torch.randn(B, C, I * H, I * W, generator=g)
+    return guide, value, weight, bias, gout
+
+
+def _oracle_grads(guide, value, weight, bias, gout, K, conv_res, hardmax):
+    offsets, pn = neighbourhood(K)
+    ts = [t.double().requires_grad_() for t in (guide, value, weight, bias)]
+    out = lao.local_attender(*ts, conv_res=conv_res, hardmax=hardmax, offsets=offsets, pn=pn)
+    (out * gout.double()).sum().backward()
+    return [t.grad for t in ts]
+
+
+def _kernel_grads(guide, value, weight, bias, gout, K, conv_res, hardmax):
+    offsets, pn = neighbourhood(K)
+    ts = [t.to(DEV).requires_grad_() for t in (guide, value, weight, bias)]
+    out = ops.local_attender(*ts, offsets, pn, conv_res=conv_res, hardmax=hardmax)
+    (out.float() * gout.to(DEV)).sum().backward()
+    return [t.grad.float().cpu() for t in ts]
+
+
+@pytest.mark.parametrize("K", [5, 9, 13, 17, 25])
+def test_gradients_vs_fp64_autograd(K, cuda_lib):
+    for (I, B, Cg, C, H, W) in [(2, 2, 16, 12, 5, 7), (1, 1, 24, 8, 6, 5), (3, 2, 8, 6, 3, 4), (2, 1, 32, 20, 1, 9)]:
+        for conv_res in (True, False):
+            case = _case(K, I, B, Cg, C, H, W, seed=K * 10 + I)
+            exp = _oracle_grads(*case, K, conv_res, False)
+            got = _kernel_grads(*case, K, conv_res, False)
+            for name, e, g in zip(("guide", "value", "weight", "bias"), exp, got):
+                err = normwise_err(g, e)
+                assert err <= 1e-4, (K, I, B, Cg, C, H, W, conv_res, name, err)
+
+
+def test_hardmax_gradient(cuda_lib):
+    """argmax selection: no gradient into the logits (guide, weight, bias);
+    the value gradient routes each output to its selected neighbour."""
+    K = 17
+    case = _case(K, 2, 2, 16, 12, 6, 7, seed=3)
+    exp = _oracle_grads(*case, K, True, True)
+    got = _kernel_grads(*case, K, True, True)
+    assert normwise_err(got[1], exp[1]) <= 1e-5
+    for g in (got[0], got[2], got[3]):
+        assert float(g.abs().max()) == 0.0
+
+
+def test_bf16_gradients(cuda_lib):
+    K = 17
+    case = _case(K, 2, 2, 64, 48, 6, 8, seed=9, dt=torch.bfloat16, wscale=0.05)
+    exp = _oracle_grads(*case, K, True, False)
+    got = _kernel_grads(*case, K, True, False)
+    for name, e, g in zip(("guide", "value", "weight", "bias"), exp, got):
+        assert normwise_err(g, e) <= 2e-2, name
+
+
+def test_module_training_step(cuda_lib):
+    """LocalAttender in a training step: autograd reaches conv1 through the
+    fused kernel, and an SGD step matches the same step through the oracle."""
+    torch.manual_seed(0)
+    K, Cg, C = 17, 64, 32
+    la = LocalAttender(Cg, K).to(DEV)
+    ref_w = la.conv1.weight.detach().cpu().double().clone().requires_grad_()
+    ref_b = la.conv1.bias.detach().cpu().double().clone().requires_grad_()
+    g = torch.Generator().manual_seed(4)
+    guide = torch.randn(2, Cg, 16, 20, generator=g)
+    value = torch.randn(2, C, 8, 10, generator=g)
+    target = torch.randn(2, C, 16, 20, generator=g)
+    loss = ((la(guide.to(DEV), value.to(DEV)) - target.to(DEV)) ** 2).mean()
+    loss.backward()
+    offsets, pn = neighbourhood(K)
+    ref = lao.local_attender(guide.double(), value.double(), ref_w.reshape(K, Cg), ref_b, offsets=offsets, pn=pn)
+    ((ref - target.double()) ** 2).mean().backward()
+    assert normwise_err(la.conv1.weight.grad.cpu().reshape(K, Cg), ref_w.grad.reshape(K, Cg)) <= 1e-4
+    assert normwise_err(la.conv1.bias.grad.cpu(), ref_b.grad) <= 1e-4
+    with torch.no_grad():  # inference afterwards still takes the cached fp32 projection path
+        out = la(guide.to(DEV), value.to(DEV))
+    assert not out.requires_grad

@@ -29,6 +29,7 @@ EXPORTED = (
     "uplift_la_last_kernel",
     "uplift_la_device_status",
     "uplift_la_test_hook",
+    "uplift_la_backward",
     # include/uplift_glue.h
     "uplift_resize_bilinear",
     "uplift_resize_nearest",
@@ -91,6 +92,9 @@ def load(build_if_missing: bool = False):
         lib.uplift_la_device_status.argtypes = [i]
         lib.uplift_la_test_hook.restype = i
         lib.uplift_la_test_hook.argtypes = [i, ctypes.c_ulonglong]
+        lib.uplift_la_backward.restype = i
+        lib.uplift_la_backward.argtypes = [vp, i64p, vp, i64p, vp, i64p, fp, fp, fp, vp, i64p, vp, i64p,
+                                           fp, fp, i, i, i, i, i, i, i, i8p, i, i, i, i, vp]
         lib.uplift_resize_bilinear.restype = i
         lib.uplift_resize_bilinear.argtypes = [vp, i64p, vp, i64p, i, i, i, i, i, i, i, i, i, vp]
         lib.uplift_resize_nearest.restype = i

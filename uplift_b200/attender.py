@@ -109,7 +109,12 @@ class LocalAttender(nn.Module):
         return _fp32_projection(self, self.conv1, self.num_connected)
 
     def forward(self, guide, value, hardmax=False):
-        w, b = self._projection()
+        if torch.is_grad_enabled() and (guide.requires_grad or value.requires_grad
+                                        or self.conv1.weight.requires_grad):
+            # training: the live parameters, so autograd reaches conv1
+            w, b = self.conv1.weight, self.conv1.bias
+        else:
+            w, b = self._projection()
         return ops.local_attender(guide, value, w, b, self.offsets, self.pn,
                                   conv_res=self.conv_res, hardmax=hardmax)
 

@@ -2,7 +2,8 @@
 
 `local_attender` (guide -> logits -> softmax -> pooled values) and
 `attender_pool` (pre-projected logits -> pooled values) launch the sm_100a
-kernels of libuplift_la.so on the current CUDA stream.  Both are also
+kernels of libuplift_la.so on the current CUDA stream; `local_attender` is
+differentiable (its backward runs the uplift_la_backward kernels).  Both are also
 registered as torch custom ops (``torch.ops.uplift_b200.*``) with fake
 implementations, so torch.compile traces them without a graph break (the
 reference's Triton module takes one, uplift/kernels/triton_attender.py:335).
@@ -132,6 +133,43 @@ def attender_pool_raw(logits: torch.Tensor, value: torch.Tensor, offsets: Sequen
     return out
 
 
+def local_attender_backward_raw(grad: torch.Tensor, guide: torch.Tensor, value: torch.Tensor,
+                                weight: torch.Tensor, bias: Optional[torch.Tensor], offsets: Sequence,
+                                pn: int, conv_res: bool = True, hardmax: bool = False,
+                                need_guide: bool = True, need_value: bool = True, need_params: bool = True):
+    """Launch uplift_la_backward: (dguide, dvalue, dweight [K, Cg] fp32,
+    dbias [K] fp32); entries not asked for are None."""
+    dev = _check_cuda(grad, guide, value)
+    B, C, H, W = value.shape
+    Cg, Ho, Wo = guide.shape[1], guide.shape[2], guide.shape[3]
+    I = _scale(Ho, Wo, H, W)
+    K = len(offsets)
+    w = weight.detach().reshape(K, -1).to(torch.float32).contiguous()
+    b = None if bias is None else bias.detach().to(torch.float32).contiguous()
+    d = _nhwc(grad.to(value.dtype))
+    g = _nhwc(guide)
+    v = _nhwc(value)
+    probs = torch.empty((B, Ho, Wo, K), dtype=torch.float32, device=dev)
+    dg = torch.empty_like(g, memory_format=torch.channels_last) if need_guide else None
+    dv = torch.empty((B, C, H, W), dtype=value.dtype, device=dev,
+                     memory_format=torch.channels_last) if need_value else None
+    dw = torch.zeros((K, Cg), dtype=torch.float32, device=dev) if need_params else None
+    db = torch.zeros((K,), dtype=torch.float32, device=dev) if (need_params and bias is not None) else None
+    lib = _native.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        rc = lib.uplift_la_backward(
+            d.data_ptr(), _native.strides(d), g.data_ptr(), _native.strides(g), v.data_ptr(), _native.strides(v),
+            w.data_ptr(), None if b is None else b.data_ptr(), probs.data_ptr(),
+            None if dg is None else dg.data_ptr(), _native.strides(dg if dg is not None else g),
+            None if dv is None else dv.data_ptr(), _native.strides(dv if dv is not None else v),
+            None if dw is None else dw.data_ptr(), None if db is None else db.data_ptr(),
+            B, Cg, C, H, W, I, K, _native.offsets_array(offsets), int(pn), int(bool(conv_res)),
+            _DTYPES[value.dtype], int(bool(hardmax)), stream)
+    _native.check(rc, "uplift_la_backward")
+    return dg, dv, dw, db
+
+
 # ----------------------------------------------------------------- custom ops
 def _pairs(flat: Sequence[int]):
     return [(flat[i], flat[i + 1]) for i in range(0, len(flat), 2)]
@@ -149,6 +187,26 @@ def _(guide, value, weight, bias, offsets, pn, conv_res, hardmax):
     B, C = value.shape[0], value.shape[1]
     return value.new_empty((B, C, guide.shape[2], guide.shape[3])).contiguous(
         memory_format=torch.channels_last)
+
+
+def _la_setup_context(ctx, inputs, output):
+    guide, value, weight, bias, offsets, pn, conv_res, hardmax = inputs
+    ctx.save_for_backward(guide, value, weight, bias)
+    ctx.offsets, ctx.pn, ctx.conv_res, ctx.hardmax = offsets, pn, conv_res, hardmax
+
+
+def _la_backward(ctx, grad):
+    guide, value, weight, bias = ctx.saved_tensors
+    ng, nv, nw, nb = ctx.needs_input_grad[:4]
+    dg, dv, dw, db = local_attender_backward_raw(
+        grad, guide, value, weight, bias, _pairs(ctx.offsets), ctx.pn, ctx.conv_res, ctx.hardmax,
+        need_guide=ng, need_value=nv, need_params=nw or nb)
+    dw = dw.reshape(weight.shape).to(weight.dtype) if nw else None
+    db = db.to(bias.dtype) if (nb and db is not None) else None
+    return dg, dv, dw, db, None, None, None, None
+
+
+torch.library.register_autograd("uplift_b200::local_attender", _la_backward, setup_context=_la_setup_context)
 
 
 @torch.library.custom_op("uplift_b200::attender_pool", mutates_args=())
