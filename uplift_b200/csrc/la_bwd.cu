@@ -11,20 +11,26 @@
 //   db_k  += sum_p dl_k
 //   dV[n][ch] = sum over (p, k) with n_k(p) = n of P_k(p) dout[p][ch]
 // Three launches: the softmax weights are recomputed into a caller-provided
-// fp32 workspace [B, Ho, Wo, K] (probs_kernel); dlogit_kernel (one thread
-// per output pixel, 128 per CTA) forms dP, dl and dg and reduces dW / db
-// over its tile in shared memory before one atomic add per entry; and
-// dvalue_kernel gathers dV per value pixel (one CTA per value row) by
-// enumerating, for every offset, the cells whose clamped neighbour is that
-// pixel -- no atomics on the large tensors.  fp32 arithmetic throughout.
+// fp32 workspace [B, Ho, Wo, K] (probs_kernel, a thread per pixel);
+// dlogit_kernel (a group of 8 lanes per unit of CPT children of one cell,
+// lanes over 16-byte channel vectors, so each dout row and each neighbour
+// value row is read once per unit) forms dP, dl and dg and reduces dW / db
+// over the CTA in shared memory before one global atomic add per entry; and
+// dvalue_window_kernel gathers dV with a sliding window: a thread owns one
+// (value row, 16-byte channel vector), sweeps the cells of the row left to
+// right and keeps the 2 pn + 1 value pixels a cell can reach in a register
+// ring, so each dout child is loaded once per offset row (no atomics on the
+// large tensors).  fp32 arithmetic throughout.
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "uplift_la.h"
 #include "la_internal.h"
@@ -32,9 +38,8 @@
 namespace ula {
 namespace bwd {
 
-constexpr int kPix = 128;       // output pixels per dlogit CTA (one thread each)
-constexpr int kThreads = 256;   // probs / dvalue CTAs
-constexpr int kGChunk = 32;     // guide channels staged per dW step
+constexpr int kThreads = 256;   // threads per CTA: probs, dvalue
+constexpr int kDThreads = 128;  // threads per CTA: dlogit
 constexpr int kMaxK = UPLIFT_LA_MAX_K;
 
 __device__ __forceinline__ float tof(float x) { return x; }
@@ -73,7 +78,23 @@ __device__ __forceinline__ void stage_weights(const Args& a, float* s_w, int nth
   }
 }
 
-template <typename T, int K>
+// 16-byte vectors of VEC storage elements.
+template <typename T, int VEC>
+struct V16 {
+  alignas(16) T e[VEC];
+  __device__ __forceinline__ void load(const T* p) {
+    if constexpr (VEC * sizeof(T) == 16) {
+      *reinterpret_cast<uint4*>(e) = __ldg(reinterpret_cast<const uint4*>(p));
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) e[i] = p[i];
+    }
+  }
+};
+
+// Softmax (or argmax one-hot) weights of every output pixel; GV guide
+// elements per load (16-byte vectors when the guide layout allows).
+template <typename T, int K, int GV>
 __global__ void __launch_bounds__(kThreads) probs_kernel(const Args a) {
   extern __shared__ float s_w[];  // [Cg][K]
   stage_weights<K>(a, s_w, kThreads);
@@ -89,10 +110,15 @@ __global__ void __launch_bounds__(kThreads) probs_kernel(const Args a) {
     float l[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) l[k] = a.bias != nullptr ? a.bias[k] : 0.f;
-    for (int c = 0; c < a.Cg; ++c) {
-      const float g = tof(gp[c]);
+    for (int c0 = 0; c0 < a.Cg; c0 += GV) {
+      V16<T, GV> gv;
+      gv.load(gp + c0);
 #pragma unroll
-      for (int k = 0; k < K; ++k) l[k] = fmaf(s_w[c * K + k], g, l[k]);
+      for (int e = 0; e < GV; ++e) {
+        const float g = tof(gv.e[e]);
+#pragma unroll
+        for (int k = 0; k < K; ++k) l[k] = fmaf(s_w[(c0 + e) * K + k], g, l[k]);
+      }
     }
     float* pp = a.probs + p * K;
     if (a.hardmax) {
@@ -117,88 +143,168 @@ __global__ void __launch_bounds__(kThreads) probs_kernel(const Args a) {
   }
 }
 
-template <typename T, int K>
-__global__ void __launch_bounds__(kPix) dlogit_kernel(const Args a) {
+// A group of kGroup lanes per unit (CPT children of one cell: the 2 x 2
+// children for I = 2, one row of 4 for I = 4, one pixel otherwise), 32 /
+// kGroup units per warp; the group's lanes stride over 16-byte channel
+// vectors, so each dout row and each neighbour value row is read once per
+// unit, and the partial dP sums need log2(kGroup) shuffle steps.  dW / db
+// are reduced per unit slot in shared memory (no same-address atomics
+// inside a warp), then once per CTA into global memory.
+constexpr int kGroup = 8;
+constexpr int kSlots = 32 / kGroup;
+
+// Per-slot dW replicas start 8 banks apart, so the four slots of a warp
+// (same k, channels sub + 8 j) hit 32 distinct banks.
+__host__ __device__ constexpr int dw_slot_stride(int K, int Cg) { return (K * Cg + 31) / 32 * 32 + 8; }
+
+template <int K>
+__host__ __device__ constexpr size_t dlogit_smem_floats(int Cg) {
+  return (size_t)Cg * K + (size_t)kSlots * dw_slot_stride(K, Cg) + (size_t)kSlots * K;
+}
+
+// Four CTAs per SM when the unit holds at most two children (<= 128
+// registers), two otherwise.
+template <typename T, int K, int CPT, int VEC>
+__global__ void __launch_bounds__(kDThreads, CPT <= 2 ? 4 : 2) dlogit_kernel(const Args a) {
   extern __shared__ float smem[];
-  float* s_w = smem;                         // [Cg][K]
-  float* s_dl = s_w + a.Cg * K;              // [kPix][K]
-  float* s_g = s_dl + kPix * K;              // [kPix][kGChunk]
-  stage_weights<K>(a, s_w, kPix);
+  const int sstride = dw_slot_stride(K, a.Cg);
+  float* s_w = smem;                          // [Cg][K]               W' (residual folded)
+  float* s_dw = s_w + a.Cg * K;               // [kSlots][sstride]     this CTA's dW, [K][Cg] per slot
+  float* s_db = s_dw + kSlots * sstride;      // [kSlots][K]
+  stage_weights<K>(a, s_w, kDThreads);
+  for (int i = threadIdx.x; i < kSlots * (sstride + K); i += kDThreads) s_dw[i] = 0.f;
+  __syncthreads();
   const T* __restrict__ dout = static_cast<const T*>(a.dout);
   const T* __restrict__ guide = static_cast<const T*>(a.guide);
   const T* __restrict__ value = static_cast<const T*>(a.value);
-  const int64_t npix = (int64_t)a.B * a.Ho * a.Wo;
-  const int64_t p = (int64_t)blockIdx.x * kPix + threadIdx.x;
-  const bool valid = p < npix;
-  int b = 0, y = 0, x = 0;
-  if (valid) {
-    x = (int)(p % a.Wo);
-    const int64_t r = p / a.Wo;
-    y = (int)(r % a.Ho);
-    b = (int)(r / a.Ho);
-  }
-  float dl[K];
+  const int lane = threadIdx.x & 31, slot = lane / kGroup, sub = lane % kGroup;
+  float* my_dw = s_dw + slot * sstride;
+  float* my_db = s_db + slot * K;
+  const int upc = (a.I * a.I) / CPT;  // units per cell
+  const int64_t num_units = (int64_t)a.B * a.H * a.W * upc;
+  const int nv = a.C / VEC;
+  const bool params = (a.dweight != nullptr || a.dbias != nullptr) && !a.hardmax;
+  const int64_t stride = (int64_t)gridDim.x * (kDThreads / 32) * kSlots;
+  // warp-uniform trip count: slots past the end run the shuffles on zeros
+  for (int64_t u0 = ((int64_t)blockIdx.x * (kDThreads / 32) + (threadIdx.x >> 5)) * kSlots; u0 < num_units;
+       u0 += stride) {
+    const int64_t u = u0 + slot;
+    const bool valid = u < num_units;
+    const int64_t uc = valid ? u : num_units - 1;
+    const int usub = (int)(uc % upc);
+    const int64_t cell = uc / upc;
+    const int cx = (int)(cell % a.W);
+    const int64_t rr = cell / a.W;
+    const int cy = (int)(rr % a.H);
+    const int b = (int)(rr / a.H);
+    int py[CPT], px[CPT];
 #pragma unroll
-  for (int k = 0; k < K; ++k) dl[k] = 0.f;
-  if (valid && !a.hardmax) {
-    const int cy = y / a.I, cx = x / a.I;
-    const T* dp = dout + b * a.d_b + y * a.d_h + x * a.d_w;
-    const T* vb = value + b * a.v_b;
-    int64_t nb[K];
-#pragma unroll
-    for (int k = 0; k < K; ++k)
-      nb[k] = clampi(cy + a.dy[k], 0, a.H - 1) * a.v_h + clampi(cx + a.dx[k], 0, a.W - 1) * a.v_w;
-    float dP[K];
-#pragma unroll
-    for (int k = 0; k < K; ++k) dP[k] = 0.f;
-    for (int ch = 0; ch < a.C; ++ch) {
-      const float d = tof(dp[ch]);
-#pragma unroll
-      for (int k = 0; k < K; ++k) dP[k] = fmaf(d, tof(vb[nb[k] + ch]), dP[k]);
+    for (int t = 0; t < CPT; ++t) {
+      const int ch = usub * CPT + t;
+      const int ci = ch / a.I;
+      py[t] = cy * a.I + ci;
+      px[t] = cx * a.I + (ch - ci * a.I);
     }
-    const float* pp = a.probs + p * K;
+    float dl[CPT][K];
+    if (!a.hardmax) {
+      const T* vb = value + b * a.v_b;
+      float dP[CPT][K];
+#pragma unroll
+      for (int t = 0; t < CPT; ++t)
+#pragma unroll
+        for (int k = 0; k < K; ++k) dP[t][k] = 0.f;
+#pragma unroll 1
+      for (int v = sub; v < nv; v += kGroup) {
+        float d[CPT][VEC];
+#pragma unroll
+        for (int t = 0; t < CPT; ++t) {
+          V16<T, VEC> dv;
+          dv.load(dout + b * a.d_b + py[t] * a.d_h + px[t] * a.d_w + v * VEC);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) d[t][e] = tof(dv.e[e]);
+        }
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          V16<T, VEC> vv;
+          vv.load(vb + clampi(cy + a.dy[k], 0, a.H - 1) * a.v_h + clampi(cx + a.dx[k], 0, a.W - 1) * a.v_w + v * VEC);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) {
+            const float x = tof(vv.e[e]);
+#pragma unroll
+            for (int t = 0; t < CPT; ++t) dP[t][k] = fmaf(d[t][e], x, dP[t][k]);
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < CPT; ++t)
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+#pragma unroll
+          for (int o = kGroup / 2; o > 0; o >>= 1) dP[t][k] += __shfl_xor_sync(0xffffffffu, dP[t][k], o);
+#pragma unroll
+      for (int t = 0; t < CPT; ++t) {
+        const float* pp = a.probs + (((int64_t)b * a.Ho + py[t]) * a.Wo + px[t]) * K;
+        float pk[K];
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          pk[k] = pp[k];
+          s = fmaf(pk[k], dP[t][k], s);
+        }
+#pragma unroll
+        for (int k = 0; k < K; ++k) dl[t][k] = pk[k] * (dP[t][k] - s);
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < CPT; ++t)
+#pragma unroll
+        for (int k = 0; k < K; ++k) dl[t][k] = 0.f;
+    }
+    if (!valid) continue;
+    // dguide (the group's lanes over guide channels) and this unit's dW / db
+    for (int c = sub; c < a.Cg; c += kGroup) {
+      float wacc[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) wacc[k] = 0.f;
+#pragma unroll
+      for (int t = 0; t < CPT; ++t) {
+        if (a.dguide != nullptr) {
+          float acc = 0.f;
+#pragma unroll
+          for (int k = 0; k < K; ++k) acc = fmaf(dl[t][k], s_w[c * K + k], acc);
+          static_cast<T*>(a.dguide)[b * a.dg_b + py[t] * a.dg_h + px[t] * a.dg_w + c] = fromf<T>(acc);
+        }
+        if (params) {
+          const float g = tof(guide[b * a.g_b + py[t] * a.g_h + px[t] * a.g_w + c]);
+#pragma unroll
+          for (int k = 0; k < K; ++k) wacc[k] = fmaf(dl[t][k], g, wacc[k]);
+        }
+      }
+      if (params) {
+#pragma unroll
+        for (int k = 0; k < K; ++k) atomicAdd(my_dw + k * a.Cg + c, wacc[k]);
+      }
+    }
+    if (params) {
+      for (int k0 = sub; k0 < K; k0 += kGroup) {
+        float acc = 0.f;
+#pragma unroll
+        for (int t = 0; t < CPT; ++t)
+#pragma unroll
+          for (int k = 0; k < K; ++k) acc += (k == k0) ? dl[t][k] : 0.f;
+        atomicAdd(my_db + k0, acc);
+      }
+    }
+  }
+  if (!params) return;
+  __syncthreads();
+  for (int i = threadIdx.x; i < K * (a.Cg + 1); i += kDThreads) {
+    const bool isw = i < K * a.Cg;
     float s = 0.f;
 #pragma unroll
-    for (int k = 0; k < K; ++k) s = fmaf(pp[k], dP[k], s);
-#pragma unroll
-    for (int k = 0; k < K; ++k) dl[k] = pp[k] * (dP[k] - s);
-  }
-#pragma unroll
-  for (int k = 0; k < K; ++k) s_dl[threadIdx.x * K + k] = dl[k];
-  __syncthreads();  // s_w staged, s_dl complete
-  if (valid && a.dguide != nullptr) {
-    T* gp = static_cast<T*>(a.dguide) + b * a.dg_b + y * a.dg_h + x * a.dg_w;
-    for (int c = 0; c < a.Cg; ++c) {
-      float acc = 0.f;
-#pragma unroll
-      for (int k = 0; k < K; ++k) acc = fmaf(dl[k], s_w[c * K + k], acc);
-      gp[c] = fromf<T>(acc);
-    }
-  }
-  if (a.hardmax || (a.dweight == nullptr && a.dbias == nullptr)) return;
-  // dW / db over this tile: guide chunks of kGChunk channels through s_g
-  const int64_t p0 = (int64_t)blockIdx.x * kPix;
-  const int tile = npix - p0 < kPix ? (int)(npix - p0) : kPix;
-  if (a.dbias != nullptr && threadIdx.x < K) {
-    float acc = 0.f;
-    for (int t = 0; t < tile; ++t) acc += s_dl[t * K + threadIdx.x];
-    atomicAdd(a.dbias + threadIdx.x, acc);
-  }
-  if (a.dweight == nullptr) return;
-  for (int c0 = 0; c0 < a.Cg; c0 += kGChunk) {
-    const int cn = min(kGChunk, a.Cg - c0);
-    __syncthreads();  // previous chunk consumed
-    if (valid) {
-      const T* gp = guide + b * a.g_b + y * a.g_h + x * a.g_w + c0;
-      for (int j = 0; j < cn; ++j) s_g[threadIdx.x * kGChunk + j] = tof(gp[j]);
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < K * cn; i += kPix) {
-      const int k = i / cn, j = i - k * cn;
-      float acc = 0.f;
-      for (int t = 0; t < tile; ++t) acc = fmaf(s_dl[t * K + k], s_g[t * kGChunk + j], acc);
-      atomicAdd(a.dweight + (size_t)k * a.Cg + c0 + j, acc);
-    }
+    for (int q = 0; q < kSlots; ++q) s += isw ? s_dw[q * sstride + i] : s_db[q * K + (i - K * a.Cg)];
+    if (isw && a.dweight != nullptr) atomicAdd(a.dweight + i, s);
+    if (!isw && a.dbias != nullptr) atomicAdd(a.dbias + (i - K * a.Cg), s);
   }
 }
 
@@ -211,70 +317,289 @@ __device__ __forceinline__ void cell_range(int n, int d, int n_len, int& lo, int
   hi = min(hi, n_len - 1);
 }
 
-template <typename T, int K>
+// dV per value pixel, general form (any offset table): one CTA per value
+// row, a thread per (pixel, channel vector), gathering P_k(p) dout[p] over
+// the children p of every cell whose offset-k neighbour is this pixel.
+template <typename T, int K, int VEC>
 __global__ void __launch_bounds__(kThreads) dvalue_kernel(const Args a) {
+  __shared__ int s_off[2 * K];  // dy, dx (read with a runtime index below)
+  if (threadIdx.x < K) {
+    s_off[threadIdx.x] = a.dy[threadIdx.x];
+    s_off[K + threadIdx.x] = a.dx[threadIdx.x];
+  }
+  __syncthreads();
   const T* __restrict__ dout = static_cast<const T*>(a.dout);
   T* __restrict__ dv = static_cast<T*>(a.dvalue);
   const int row = blockIdx.x;  // (b, ny)
   const int ny = row % a.H, b = row / a.H;
-  const int items = a.W * a.C;
+  const int nv = a.C / VEC;
+  const int items = a.W * nv;
+  const T* db = dout + b * a.d_b;
+  const float* pb = a.probs + (int64_t)b * a.Ho * a.Wo * K;
   for (int i = threadIdx.x; i < items; i += kThreads) {
-    const int nx = i / a.C, ch = i - nx * a.C;
-    float acc = 0.f;
+    const int nx = i / nv, c0 = (i - nx * nv) * VEC;
+    float acc[VEC];
 #pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
+#pragma unroll 1
     for (int k = 0; k < K; ++k) {
       int ylo, yhi, xlo, xhi;
-      cell_range(ny, a.dy[k], a.H, ylo, yhi);
-      cell_range(nx, a.dx[k], a.W, xlo, xhi);
-      for (int cy = ylo; cy <= yhi; ++cy)
-        for (int cx = xlo; cx <= xhi; ++cx)
-          for (int iy = 0; iy < a.I; ++iy)
-            for (int ix = 0; ix < a.I; ++ix) {
-              const int y = cy * a.I + iy, x = cx * a.I + ix;
-              const float pk = a.probs[(((int64_t)b * a.Ho + y) * a.Wo + x) * K + k];
-              if (pk != 0.f) acc = fmaf(pk, tof(dout[b * a.d_b + y * a.d_h + x * a.d_w + ch]), acc);
-            }
+      cell_range(ny, s_off[k], a.H, ylo, yhi);
+      cell_range(nx, s_off[K + k], a.W, xlo, xhi);
+      for (int y = ylo * a.I; y < (yhi + 1) * a.I; ++y)
+        for (int x = xlo * a.I; x < (xhi + 1) * a.I; ++x) {
+          const float pk = pb[((int64_t)y * a.Wo + x) * K + k];
+          if (pk != 0.f) {
+            V16<T, VEC> d;
+            d.load(db + y * a.d_h + x * a.d_w + c0);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) acc[e] = fmaf(pk, tof(d.e[e]), acc[e]);
+          }
+        }
     }
-    dv[b * a.dv_b + ny * a.dv_h + nx * a.dv_w + ch] = fromf<T>(acc);
+    T* out = dv + b * a.dv_b + ny * a.dv_h + nx * a.dv_w + c0;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) out[e] = fromf<T>(acc[e]);
   }
 }
 
-template <typename T, int K>
-int launch(const Args& a, cudaStream_t stream) {
+// The reference's offset tables (uplift/uplift.py:746-760), as the map
+// (dy, dx) -> k (-1 where the table has no such offset) and their reach pn.
+// Used as compile-time constants by the sliding-window dV kernel when the
+// caller passes exactly these tables.
+template <int K>
+__host__ __device__ constexpr int nbh_pn() { return (K == 5 || K == 9) ? 1 : 2; }
+
+template <int K>
+__host__ __device__ constexpr int nbh_k(int dy, int dx) {
+  const int ady = dy < 0 ? -dy : dy, adx = dx < 0 ? -dx : dx;
+  if (K == 25) return (ady <= 2 && adx <= 2) ? (dy + 2) * 5 + dx + 2 : -1;
+  if (K == 9) return (ady <= 1 && adx <= 1) ? (dy + 1) * 3 + dx + 1 : -1;
+  if (K == 5) {
+    if (dy == 0) return adx <= 1 ? 2 + dx : -1;
+    return (ady == 1 && dx == 0) ? (dy < 0 ? 0 : 4) : -1;
+  }
+  if (K == 13) {
+    if (dy == 0) return adx <= 2 ? 6 + dx : -1;
+    if (ady == 1) return adx <= 1 ? (dy < 0 ? 1 : 9) + dx + 1 : -1;
+    return (ady == 2 && dx == 0) ? (dy < 0 ? 0 : 12) : -1;
+  }
+  if (K == 17) {
+    if (dy == 0) return adx <= 2 ? 8 + dx : -1;
+    if (ady == 1) return adx <= 1 ? (dy < 0 ? 3 : 11) + dx + 1 : -1;
+    return (ady == 2 && (dx == -2 || dx == 0 || dx == 2)) ? (dy < 0 ? 0 : 14) + (dx + 2) / 2 : -1;
+  }
+  return -1;
+}
+
+// dV with a sliding window (the reference's offset table for K).  A thread
+// owns (b, value row ny, channel vector v, segment [x0, x1) of value
+// columns) and sweeps the cells cx of [x0 - PN, x1 + PN).  Cell cx
+// contributes to the value pixels clamp(cx + dx) in [cx - PN, cx + PN]; ring
+// slot s holds the pixel cx - PN + s, so after cell cx the pixel cx - PN is
+// complete, is written and the ring shifts by one.  Rows: for each dy the
+// cells whose clamped row neighbour is ny (cell_range, a single row away
+// from the top and bottom edges); the I x I children of each are loaded once
+// and used for every dx of that dy.  Cells within PN of the left or right
+// edge take a runtime slot (clamped dx) through a compile-time select.
+template <typename T, int K, int VEC, int IT>
+__global__ void __launch_bounds__(kThreads, 1) dvalue_window_kernel(const Args a, int seg_len, int nseg) {
+  constexpr int PN = nbh_pn<K>();
+  constexpr int S = 2 * PN + 1;
+  constexpr int ITc = IT > 0 ? IT : 1;  // child grid of the unrolled path
+  const int nv = a.C / VEC;
+  const int64_t t = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  if (t >= (int64_t)a.B * a.H * nseg * nv) return;
+  const int v = (int)(t % nv);
+  int64_t r = t / nv;
+  const int seg = (int)(r % nseg);
+  r /= nseg;
+  const int ny = (int)(r % a.H), b = (int)(r / a.H);
+  const int x0 = seg * seg_len, x1 = min(a.W, x0 + seg_len);
+  if (x0 >= x1) return;
+  const T* __restrict__ db = static_cast<const T*>(a.dout) + b * a.d_b + v * VEC;
+  const float* __restrict__ pb = a.probs + (int64_t)b * a.Ho * a.Wo * K;
+  T* __restrict__ out = static_cast<T*>(a.dvalue) + b * a.dv_b + ny * a.dv_h + v * VEC;
+  const int I = IT > 0 ? IT : a.I;
+  const bool row_inner = IT > 0 && ny >= PN && ny < a.H - PN;
+  float ring[S][VEC];
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) ring[s][e] = 0.f;
+
+  // ring[slot(dx)] += P_k(child) dout(child) for every dx of offset row i
+  auto add_child = [&](auto inner, int i, int cx, int y, int x) {
+    V16<T, VEC> dv;
+    dv.load(db + y * a.d_h + x * a.d_w);
+    float d[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) d[e] = tof(dv.e[e]);
+    const float* pp = pb + ((int64_t)y * a.Wo + x) * K;
+#pragma unroll
+    for (int j = 0; j < S; ++j) {
+      const int k = nbh_k<K>(i - PN, j - PN);
+      if (k < 0) continue;
+      const float pk = pp[k];
+      if (decltype(inner)::value) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) ring[j][e] = fmaf(pk, d[e], ring[j][e]);
+      } else {
+        const int slot = clampi(cx + j - PN, 0, a.W - 1) - cx + PN;
+#pragma unroll
+        for (int q = 0; q < S; ++q)
+          if (q == slot) {
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) ring[q][e] = fmaf(pk, d[e], ring[q][e]);
+          }
+      }
+    }
+  };
+  auto step = [&](auto inner, int cx) {
+    if (row_inner) {
+#pragma unroll
+      for (int i = 0; i < S; ++i) {
+        const int cy = ny - (i - PN);
+#pragma unroll
+        for (int ch = 0; ch < ITc * ITc; ++ch) add_child(inner, i, cx, cy * ITc + ch / ITc, cx * ITc + ch % ITc);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < S; ++i) {
+        int lo, hi;
+        cell_range(ny, i - PN, a.H, lo, hi);
+#pragma unroll 1
+        for (int cy = lo; cy <= hi; ++cy)
+#pragma unroll 1
+          for (int ch = 0; ch < I * I; ++ch) add_child(inner, i, cx, cy * I + ch / I, cx * I + ch % I);
+      }
+    }
+    const int nx = cx - PN;
+    if (nx >= x0) {
+      T* o = out + nx * a.dv_w;
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = fromf<T>(ring[0][e]);
+    }
+#pragma unroll
+    for (int s = 0; s + 1 < S; ++s)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) ring[s][e] = ring[s + 1][e];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) ring[S - 1][e] = 0.f;
+  };
+  using Edge = std::integral_constant<bool, false>;
+  using Inner = std::integral_constant<bool, true>;
+  const int c0 = max(0, x0 - PN), cend = min(a.W, x1 + PN);
+  const int i0 = min(max(c0, PN), cend), i1 = max(min(cend, a.W - PN), i0);
+  for (int cx = c0; cx < i0; ++cx) step(Edge{}, cx);
+#pragma unroll 1
+  for (int cx = i0; cx < i1; ++cx) step(Inner{}, cx);
+  for (int cx = i1; cx < cend; ++cx) step(Edge{}, cx);
+  // pixels the sweep did not reach cx = nx + PN for (right edge of the map)
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    const int nx = cend - PN + s;
+    if (nx >= x0 && nx < x1) {
+      T* o = out + nx * a.dv_w;
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = fromf<T>(ring[s][e]);
+    }
+  }
+}
+
+struct Plan {
+  int window;    // 1: sliding-window dV (reference offset table); 0: general dV kernel
+  int seg_len;   // value columns per window thread
+  int nseg;
+};
+
+template <typename T, int K, int CPT, int VEC, int GV>
+int launch_cv(const Args& a, const Plan& plan, cudaStream_t stream) {
   const int64_t npix = (int64_t)a.B * a.Ho * a.Wo;
   if (npix == 0) return UPLIFT_LA_OK;
   const size_t smem_p = sizeof(float) * (size_t)a.Cg * K;
-  const size_t smem_d = sizeof(float) * ((size_t)a.Cg * K + (size_t)kPix * K + (size_t)kPix * kGChunk);
-  int dev = 0, optin = 0;
+  const size_t smem_d = sizeof(float) * dlogit_smem_floats<K>(a.Cg);
+  int dev = 0, optin = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return fail(UPLIFT_LA_ERR_CUDA, "device query failed");
   if (smem_d > (size_t)optin) return fail(UPLIFT_LA_ERR_SHAPE, "backward: Cg=%d needs too much shared memory", a.Cg);
-  cudaError_t e = cudaFuncSetAttribute(probs_kernel<T, K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_p);
+  cudaError_t e = cudaFuncSetAttribute(probs_kernel<T, K, GV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_p);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(dlogit_kernel<T, K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_d);
+    e = cudaFuncSetAttribute(dlogit_kernel<T, K, CPT, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_d);
   if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  const int64_t pblocks = std::min<int64_t>((npix + kThreads - 1) / kThreads, 148ll * 16);
-  probs_kernel<T, K><<<(unsigned)pblocks, kThreads, smem_p, stream>>>(a);
-  const int64_t dblocks = (npix + kPix - 1) / kPix;
-  if (dblocks >= (1ll << 31)) return fail(UPLIFT_LA_ERR_SHAPE, "backward: too many pixels");
-  if (a.dguide != nullptr || a.dweight != nullptr || a.dbias != nullptr)
-    dlogit_kernel<T, K><<<(unsigned)dblocks, kPix, smem_d, stream>>>(a);
-  if (a.dvalue != nullptr && a.B * (int64_t)a.H > 0)
-    dvalue_kernel<T, K><<<(unsigned)(a.B * (int64_t)a.H), kThreads, 0, stream>>>(a);
+  const int64_t pblocks = std::min<int64_t>((npix + kThreads - 1) / kThreads, (int64_t)sms * 16);
+  probs_kernel<T, K, GV><<<(unsigned)pblocks, kThreads, smem_p, stream>>>(a);
+  if (a.dguide != nullptr || a.dweight != nullptr || a.dbias != nullptr) {
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, dlogit_kernel<T, K, CPT, VEC>, kDThreads, smem_d) !=
+            cudaSuccess || occ < 1)
+      occ = 1;
+    const int64_t units = (int64_t)a.B * a.H * a.W * ((a.I * a.I) / CPT);
+    const int64_t per_cta = (kDThreads / 32) * kSlots;
+    const int64_t dblocks = std::min<int64_t>((units + per_cta - 1) / per_cta, (int64_t)sms * occ);
+    dlogit_kernel<T, K, CPT, VEC><<<(unsigned)dblocks, kDThreads, smem_d, stream>>>(a);
+  }
+  if (a.dvalue != nullptr && a.B * (int64_t)a.H > 0) {
+    if (plan.window) {
+      const int64_t threads = (int64_t)a.B * a.H * plan.nseg * (a.C / VEC);
+      const int64_t blocks = (threads + kThreads - 1) / kThreads;
+      if (blocks >= (1ll << 31)) return fail(UPLIFT_LA_ERR_SHAPE, "backward: grid too large");
+      const unsigned nb = (unsigned)blocks;
+      if (a.I == 2) dvalue_window_kernel<T, K, VEC, 2><<<nb, kThreads, 0, stream>>>(a, plan.seg_len, plan.nseg);
+      else dvalue_window_kernel<T, K, VEC, 0><<<nb, kThreads, 0, stream>>>(a, plan.seg_len, plan.nseg);
+    } else {
+      if (a.B * (int64_t)a.H >= (1ll << 31)) return fail(UPLIFT_LA_ERR_SHAPE, "backward: too many value rows");
+      dvalue_kernel<T, K, VEC><<<(unsigned)(a.B * (int64_t)a.H), kThreads, 0, stream>>>(a);
+    }
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "backward launch: %s", cudaGetErrorString(e));
   return UPLIFT_LA_OK;
 }
 
+// Children per dlogit unit: 4 for I = 2 and I = 4 (2 with ULA_BWD_CPT=2),
+// 2 for other even I, else 1.  16-byte vectors when the channel counts and
+// alignment allow them (vec: dout / value / dvalue; gvec: guide).
+inline int unit_children(int I) {
+  static const int env = [] {
+    const char* s = getenv("ULA_BWD_CPT");
+    return s != nullptr ? atoi(s) : 4;
+  }();
+  if (I % 2 != 0) return 1;
+  return (env != 2 && (I == 2 || I == 4)) ? 4 : 2;
+}
+
+template <typename T, int K, int CPT, int VEC>
+int launch_g(const Args& a, const Plan& plan, bool gvec, cudaStream_t stream) {
+  constexpr int V = 16 / sizeof(T);
+  return gvec ? launch_cv<T, K, CPT, VEC, V>(a, plan, stream) : launch_cv<T, K, CPT, VEC, 1>(a, plan, stream);
+}
+
+template <typename T, int K, int VEC>
+int launch_c(const Args& a, const Plan& plan, bool gvec, cudaStream_t stream) {
+  switch (unit_children(a.I)) {
+    case 4: return launch_g<T, K, 4, VEC>(a, plan, gvec, stream);
+    case 2: return launch_g<T, K, 2, VEC>(a, plan, gvec, stream);
+    default: return launch_g<T, K, 1, VEC>(a, plan, gvec, stream);
+  }
+}
+
+template <typename T, int K>
+int launch(const Args& a, const Plan& plan, bool vec, bool gvec, cudaStream_t stream) {
+  constexpr int V = 16 / sizeof(T);
+  return vec ? launch_c<T, K, V>(a, plan, gvec, stream) : launch_c<T, K, 1>(a, plan, gvec, stream);
+}
+
 template <typename T>
-int launch_k(const Args& a, int K, cudaStream_t stream) {
+int launch_k(const Args& a, const Plan& plan, int K, bool vec, bool gvec, cudaStream_t stream) {
   switch (K) {
-    case 5: return launch<T, 5>(a, stream);
-    case 9: return launch<T, 9>(a, stream);
-    case 13: return launch<T, 13>(a, stream);
-    case 17: return launch<T, 17>(a, stream);
-    case 25: return launch<T, 25>(a, stream);
+    case 5: return launch<T, 5>(a, plan, vec, gvec, stream);
+    case 9: return launch<T, 9>(a, plan, vec, gvec, stream);
+    case 13: return launch<T, 13>(a, plan, vec, gvec, stream);
+    case 17: return launch<T, 17>(a, plan, vec, gvec, stream);
+    case 25: return launch<T, 25>(a, plan, vec, gvec, stream);
     default: return fail(UPLIFT_LA_ERR_SHAPE, "backward: K=%d unsupported (5, 9, 13, 17, 25)", K);
   }
 }
@@ -334,10 +659,47 @@ extern "C" int uplift_la_backward(const void* dout, const int64_t dout_strides[4
   a.B = B; a.Cg = Cg; a.C = C; a.H = H; a.W = W; a.I = I; a.Ho = I * H; a.Wo = I * W;
   a.conv_res = conv_res ? 1 : 0;
   a.hardmax = hardmax ? 1 : 0;
+  // 16-byte channel vectors for dout / value / dvalue when C and alignment allow
+  const int ve = dtype == UPLIFT_LA_F32 ? 4 : 8;
+  auto a16 = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  bool vec = C % ve == 0 && a16(dout) && a16(value) && a16(dvalue);
+  const int64_t vst[6] = {a.d_b, a.d_h, a.d_w, a.v_b, a.v_h, a.v_w};
+  for (int i = 0; i < 6; ++i) vec = vec && vst[i] % ve == 0;
+  if (dvalue != nullptr) vec = vec && a.dv_b % ve == 0 && a.dv_h % ve == 0 && a.dv_w % ve == 0;
+  const bool gvec = Cg % ve == 0 && a16(guide) && a.g_b % ve == 0 && a.g_h % ve == 0 && a.g_w % ve == 0;
+  // sliding-window dV when the offsets are the reference's table for K; row
+  // segments sized so that about 2048 threads per SM are busy
+  bwd::Plan plan{0, W, 1};
+  bool canonical = true;
+  for (int k = 0; k < K; ++k) {
+    int kk = -1;
+    switch (K) {
+      case 5: kk = bwd::nbh_k<5>(a.dy[k], a.dx[k]); break;
+      case 9: kk = bwd::nbh_k<9>(a.dy[k], a.dx[k]); break;
+      case 13: kk = bwd::nbh_k<13>(a.dy[k], a.dx[k]); break;
+      case 17: kk = bwd::nbh_k<17>(a.dy[k], a.dx[k]); break;
+      case 25: kk = bwd::nbh_k<25>(a.dy[k], a.dx[k]); break;
+      default: break;
+    }
+    canonical = canonical && kk == k;
+  }
+  if (canonical && W > 0) {
+    plan.window = 1;
+    const int pn_k = (K == 5 || K == 9) ? 1 : 2;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t rows = (int64_t)B * H * (C / (vec ? ve : 1));
+    const int64_t want = (int64_t)sms * 2048;
+    int nseg = rows >= want ? 1 : (int)std::min<int64_t>((want + rows - 1) / rows, W);
+    const int min_len = 8 * pn_k;
+    if (nseg > 1 && (W + nseg - 1) / nseg < min_len) nseg = std::max(1, W / min_len);
+    plan.seg_len = (W + nseg - 1) / nseg;
+    plan.nseg = (W + plan.seg_len - 1) / plan.seg_len;
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case UPLIFT_LA_F32: return bwd::launch_k<float>(a, K, s);
-    case UPLIFT_LA_BF16: return bwd::launch_k<__nv_bfloat16>(a, K, s);
-    default: return bwd::launch_k<__half>(a, K, s);
+    case UPLIFT_LA_F32: return bwd::launch_k<float>(a, plan, K, vec, gvec, s);
+    case UPLIFT_LA_BF16: return bwd::launch_k<__nv_bfloat16>(a, plan, K, vec, gvec, s);
+    default: return bwd::launch_k<__half>(a, plan, K, vec, gvec, s);
   }
 }
