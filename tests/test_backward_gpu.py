@@ -95,3 +95,34 @@ def test_module_training_step(cuda_lib):
     with torch.no_grad():  # inference afterwards still takes the cached fp32 projection path
         out = la(guide.to(DEV), value.to(DEV))
     assert not out.requires_grad
+
+
+@pytest.mark.parametrize("K", [9, 17, 25])
+def test_gradients_permuted_offsets(K, cuda_lib):
+    """An offset table in another order than the reference's takes the
+    general dV kernel (runtime offsets) instead of the sliding window."""
+    offsets, pn = neighbourhood(K)
+    perm = torch.randperm(K, generator=torch.Generator().manual_seed(K)).tolist()
+    offsets = [offsets[i] for i in perm]
+    for (I, B, Cg, C, H, W) in [(2, 2, 16, 12, 5, 7), (1, 1, 8, 6, 4, 3)]:
+        guide, value, weight, bias, gout = _case(K, I, B, Cg, C, H, W, seed=K + I)
+        ts = [t.double().requires_grad_() for t in (guide, value, weight, bias)]
+        out = lao.local_attender(*ts, offsets=offsets, pn=pn)
+        (out * gout.double()).sum().backward()
+        tg = [t.to(DEV).requires_grad_() for t in (guide, value, weight, bias)]
+        o = ops.local_attender(*tg, offsets, pn)
+        (o.float() * gout.to(DEV)).sum().backward()
+        for name, e, g in zip(("guide", "value", "weight", "bias"), [t.grad for t in ts], [t.grad for t in tg]):
+            assert normwise_err(g.float().cpu(), e) <= 1e-4, (K, I, name)
+
+
+@pytest.mark.parametrize("I", [4, 6])
+def test_gradients_other_factors(I, cuda_lib):
+    """Units of four children in a row (I = 4) and of two (I = 6)."""
+    K = 17
+    for dt, tol in ((torch.float32, 1e-4), (torch.bfloat16, 2e-2)):
+        case = _case(K, I, 2, 32, 16, 3, 4, seed=I, dt=dt, wscale=0.05)
+        exp = _oracle_grads(*case, K, True, False)
+        got = _kernel_grads(*case, K, True, False)
+        for name, e, g in zip(("guide", "value", "weight", "bias"), exp, got):
+            assert normwise_err(g, e) <= tol, (I, dt, name)
