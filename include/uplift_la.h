@@ -121,6 +121,37 @@ int uplift_la_backward(const void* dout, const int64_t dout_strides[4],
                        const int8_t* offsets, int pn, int conv_res, int dtype, int hardmax,
                        void* stream);
 
+/*
+ * uplift_la_backward for callers that cannot allocate device memory: the
+ * same arguments and results, minus the `probs` workspace.  It suits a
+ * host whose memory pool owns all device memory, a caller that must not let
+ * cudaMalloc / cudaFree synchronise the device in the middle of its work,
+ * and an FFI binding that has no device allocator.  No counterpart in the
+ * reference (its backward is PyTorch autograd, which allocates freely).
+ *
+ * The workspace is a fixed array of UPLIFT_LA_NOALLOC_MAX_PROBS floats
+ * (32 MiB) inside the library, which every GPU that loads the library
+ * holds until the process exits.  Calls with B*(I*H)*(I*W)*K above that
+ * maximum fail with UPLIFT_LA_ERR_SHAPE and launch nothing.  The first call
+ * on a device looks the array's device address up (cudaGetSymbolAddress):
+ * make that first call before any stream capture.  All calls share the one
+ * array: calls whose kernels overlap on the GPU (other streams, other host
+ * threads) race on it, so serialise them.  Every call rewrites the part it
+ * reads; dweight / dbias still accumulate into the caller's zeroed outputs.
+ * Nothing here calls cudaMalloc, cudaFree or an allocating library routine.
+ */
+#define UPLIFT_LA_NOALLOC_MAX_PROBS (8 * 1024 * 1024)
+int uplift_la_backward_noalloc(const void* dout, const int64_t dout_strides[4],
+                               const void* guide, const int64_t guide_strides[4],
+                               const void* value, const int64_t value_strides[4],
+                               const float* weight, const float* bias,
+                               void* dguide, const int64_t dguide_strides[4],
+                               void* dvalue, const int64_t dvalue_strides[4],
+                               float* dweight, float* dbias,
+                               int B, int Cg, int C, int H, int W, int I, int K,
+                               const int8_t* offsets, int pn, int conv_res, int dtype, int hardmax,
+                               void* stream);
+
 /* Kernel selection for uplift_la_forward (process-wide; default AUTO).
  * AUTO picks a tensor-core kernel (tcgen05 MMA, TMEM accumulators, TMA)
  * when one applies -- bf16/fp16 storage, I = 2, Cg = 64, C a multiple of 64

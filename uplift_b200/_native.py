@@ -17,6 +17,7 @@ F32, BF16, F16 = 0, 1, 2
 OK, ERR_ARG, ERR_SHAPE, ERR_LAYOUT, ERR_OFFSETS, ERR_CUDA, ERR_NO_DEVICE = range(7)
 MAX_K = 25
 MAX_PN = 4
+NOALLOC_MAX_PROBS = 8 * 1024 * 1024  # floats, UPLIFT_LA_NOALLOC_MAX_PROBS
 
 # every symbol include/uplift_la.h declares
 EXPORTED = (
@@ -30,6 +31,7 @@ EXPORTED = (
     "uplift_la_device_status",
     "uplift_la_test_hook",
     "uplift_la_backward",
+    "uplift_la_backward_noalloc",
     # include/uplift_glue.h
     "uplift_resize_bilinear",
     "uplift_resize_nearest",
@@ -95,6 +97,9 @@ def load(build_if_missing: bool = False):
         lib.uplift_la_backward.restype = i
         lib.uplift_la_backward.argtypes = [vp, i64p, vp, i64p, vp, i64p, fp, fp, fp, vp, i64p, vp, i64p,
                                            fp, fp, i, i, i, i, i, i, i, i8p, i, i, i, i, vp]
+        lib.uplift_la_backward_noalloc.restype = i
+        lib.uplift_la_backward_noalloc.argtypes = [vp, i64p, vp, i64p, vp, i64p, fp, fp, vp, i64p, vp, i64p,
+                                                   fp, fp, i, i, i, i, i, i, i, i8p, i, i, i, i, vp]
         lib.uplift_resize_bilinear.restype = i
         lib.uplift_resize_bilinear.argtypes = [vp, i64p, vp, i64p, i, i, i, i, i, i, i, i, i, vp]
         lib.uplift_resize_nearest.restype = i

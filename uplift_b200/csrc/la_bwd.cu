@@ -30,6 +30,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 #include <type_traits>
 
 #include "uplift_la.h"
@@ -702,4 +703,75 @@ extern "C" int uplift_la_backward(const void* dout, const int64_t dout_strides[4
     case UPLIFT_LA_BF16: return bwd::launch_k<__nv_bfloat16>(a, plan, K, vec, gvec, s);
     default: return bwd::launch_k<__half>(a, plan, K, vec, gvec, s);
   }
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free backward: the softmax-weight workspace lives in a fixed
+// array of this library instead of caller memory, for callers that cannot
+// allocate device memory (see include/uplift_la.h).  Host code reaches the
+// array only through the device address that cudaGetSymbolAddress returns
+// for the current device (the array's name on the host is a stand-in, not a
+// device address); it is looked up once per device and cached.
+namespace {
+
+static __device__ __align__(256) float g_noalloc_probs[UPLIFT_LA_NOALLOC_MAX_PROBS];
+
+constexpr int kNoallocDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoallocDevices] = {};
+
+// Device address of g_noalloc_probs on the current device, or null (error set).
+float* noalloc_workspace() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    ula::fail(UPLIFT_LA_ERR_CUDA, "uplift_la_backward_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (dev >= 0 && dev < kNoallocDevices && g_noalloc_ptr[dev] != nullptr) return g_noalloc_ptr[dev];
+  float* ptr = nullptr;
+  e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_noalloc_probs);
+  if (e != cudaSuccess || ptr == nullptr) {
+    ula::fail(UPLIFT_LA_ERR_CUDA, "uplift_la_backward_noalloc: cudaGetSymbolAddress on device %d: %s", dev,
+              cudaGetErrorString(e));
+    return nullptr;
+  }
+  if (dev >= 0 && dev < kNoallocDevices) g_noalloc_ptr[dev] = ptr;
+  return ptr;
+}
+
+}  // namespace
+
+extern "C" int uplift_la_backward_noalloc(const void* dout, const int64_t dout_strides[4],
+                                          const void* guide, const int64_t guide_strides[4],
+                                          const void* value, const int64_t value_strides[4],
+                                          const float* weight, const float* bias,
+                                          void* dguide, const int64_t dguide_strides[4],
+                                          void* dvalue, const int64_t dvalue_strides[4],
+                                          float* dweight, float* dbias,
+                                          int B, int Cg, int C, int H, int W, int I, int K,
+                                          const int8_t* offsets, int pn, int conv_res, int dtype, int hardmax,
+                                          void* stream) {
+  using namespace ula;
+  if (B < 0 || H < 0 || W < 0 || I < 1 || K < 1 || K > UPLIFT_LA_MAX_K)
+    return fail(UPLIFT_LA_ERR_SHAPE, "uplift_la_backward_noalloc: bad sizes B=%d H=%d W=%d I=%d K=%d", B, H, W, I,
+                K);
+  // B * (I*H) * (I*W) * K floats, checked factor by factor against the maximum
+  const long long cap = UPLIFT_LA_NOALLOC_MAX_PROBS;
+  long long need = 1;
+  const long long f[6] = {B, I, H, I, W, K};
+  for (int i = 0; i < 6 && need > 0; ++i) {
+    need = f[i] == 0 ? 0 : (need > cap / f[i] ? cap + 1 : need * f[i]);
+  }
+  if (need > cap)
+    return fail(UPLIFT_LA_ERR_SHAPE,
+                "uplift_la_backward_noalloc: workspace B*(I*H)*(I*W)*K exceeds the fixed maximum of %lld floats "
+                "(UPLIFT_LA_NOALLOC_MAX_PROBS); use uplift_la_backward with a caller workspace",
+                cap);
+  float* probs = noalloc_workspace();
+  if (probs == nullptr) return UPLIFT_LA_ERR_CUDA;
+  return uplift_la_backward(dout, dout_strides, guide, guide_strides, value, value_strides, weight, bias, probs,
+                            dguide, dguide_strides, dvalue, dvalue_strides, dweight, dbias, B, Cg, C, H, W, I, K,
+                            offsets, pn, conv_res, dtype, hardmax, stream);
 }
