@@ -271,6 +271,9 @@ def run_ours(args, world, rank, local):
     # ---- fp32 attender configurations (standalone K=9 call, SD1.5-VAE levels)
     fp32 = None if args.no_fp32 else run_fp32_configs(dev, stream, peak)
 
+    # ---- attender backward (training) on the same four levels
+    bwd = None if args.no_backward else run_backward(dev, stream, peak, B_PER_GPU)
+
     # ---- CPU baseline (rank 0, N=1 only): reference algorithm on host cores
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -310,6 +313,8 @@ def run_ours(args, world, rank, local):
         result["upsampler_other_configs"] = models
     if fp32 is not None:
         result["fp32_configs"] = fp32
+    if bwd is not None:
+        result["backward"] = bwd
     if cpu is not None:
         result["cpu_baseline"] = cpu
     return result
@@ -368,6 +373,56 @@ def run_fp32_configs(dev, stream, peak, reps=20):
     out["note"] = ("fp32 storage; CUDA-graph replays of one call, median of 5; bytes = algorithmic "
                    "(guide + output + value once); frac against the measured HBM copy peak")
     return out
+
+
+def run_backward(dev, stream, peak, images, reps=5):
+    """Device time of the attender backward (training; uplift_la_backward:
+    dguide, dvalue, dweight, dbias) on the four levels of the chain above,
+    bf16, `images` per GPU, random-init LocalAttender(64, 17), N(0,1) guide /
+    value / output gradient.  Eager calls (each allocates its outputs and
+    workspace from torch's cache), median of `reps` after 2 warm calls.
+    Algorithmic bytes per output pixel: dout + guide read, dguide written
+    ((C + 2 Cg) * 2), the fp32 softmax workspace written once and read twice
+    (12 K), value read and dvalue written once per value pixel (2 C * 2 / 4)."""
+    from uplift_b200 import ops
+    from uplift_b200.attender import LocalAttender, neighbourhood
+
+    offsets, pn = neighbourhood(K_NBR)
+    torch.manual_seed(0)
+    la = LocalAttender(CG, K_NBR).to(dev)
+    w = la.conv1.weight.detach().reshape(K_NBR, CG).float()
+    b = la.conv1.bias.detach().float()
+    g = torch.Generator().manual_seed(0)
+    cl = torch.channels_last
+    bpp = (C + 2 * CG) * ELEM + 12 * K_NBR + 2 * C * ELEM / 4
+    levels, tot_ms, tot_px = [], 0.0, 0
+    with torch.cuda.stream(stream):
+        for co, fo in LEVELS:
+            guide = torch.randn(images, CG, fo, fo, generator=g).to(torch.bfloat16).to(dev).contiguous(memory_format=cl)
+            value = torch.randn(images, C, co, co, generator=g).to(torch.bfloat16).to(dev).contiguous(memory_format=cl)
+            dout = torch.randn(images, C, fo, fo, generator=g).to(torch.bfloat16).to(dev).contiguous(memory_format=cl)
+            for _ in range(2):
+                ops.local_attender_backward_raw(dout, guide, value, w, b, offsets, pn)
+            times = []
+            for _ in range(reps):
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+                ev[0].record(stream)
+                ops.local_attender_backward_raw(dout, guide, value, w, b, offsets, pn)
+                ev[1].record(stream)
+                ev[1].synchronize()
+                times.append(ev[0].elapsed_time(ev[1]))
+            ms = statistics.median(times)
+            px = images * fo * fo
+            tot_ms += ms
+            tot_px += px
+            levels.append({"level": f"{co}^2->{fo}^2", "ms": round(ms, 4), "Mpix_s": round(px / ms / 1e3, 1),
+                           "GB_s": round(px * bpp / ms / 1e6, 1)})
+            del guide, value, dout
+    return {"levels": levels, "ms_chain": round(tot_ms, 4), "Mpix_s_chain": round(tot_px / tot_ms / 1e3, 1),
+            "frac_of_peak_chain": round(tot_px * bpp / tot_ms / 1e6 / peak, 4), "algo_bytes_per_pixel": bpp,
+            "launches_per_level": 3, "dtype": "bf16", "images": images,
+            "note": "probs / dlogit / dvalue kernels; eager calls, median of 5; "
+                    "frac against the measured HBM copy peak"}
 
 
 def run_e2e(la, host, dev, stream, world, args, mpix_step):
@@ -627,6 +682,9 @@ def main():
     ap.add_argument("--no-fp32", action="store_true", help="skip the fp32 attender configurations")
     ap.add_argument("--only-fp32", action="store_true",
                     help="run only the fp32 attender configurations (profiling captures)")
+    ap.add_argument("--no-backward", action="store_true", help="skip the attender backward pass")
+    ap.add_argument("--only-backward", action="store_true",
+                    help="run only the attender backward pass (profiling captures)")
     ap.add_argument("--only-upsampler", action="store_true",
                     help="run only the whole-upsampler pass (profiling captures)")
     ap.add_argument("--images", type=int, default=8,
@@ -647,6 +705,9 @@ def main():
         if args.only_fp32:
             dev = torch.device("cuda", local)
             res = {"fp32_configs": run_fp32_configs(dev, torch.cuda.current_stream(dev), load_peaks()[0])}
+        elif args.only_backward:
+            dev = torch.device("cuda", local)
+            res = {"backward": run_backward(dev, torch.cuda.current_stream(dev), load_peaks()[0], B_PER_GPU)}
         elif args.only_upsampler:
             dev = torch.device("cuda", local)
             res = {"upsampler": run_upsampler(dev, torch.cuda.current_stream(dev), world, rank, args, outsize=1022)}

@@ -210,29 +210,76 @@ __global__ void __launch_bounds__(kDThreads, CPT <= 2 ? 4 : 2) dlogit_kernel(con
     if (!a.hardmax) {
       const T* vb = value + b * a.v_b;
       float dP[CPT][K];
+      if constexpr (sizeof(T) == 2) {
+        // 16-bit storage: children in pairs (t0, t1), one packed FMA updates
+        // dP[t0][k] and dP[t1][k] with (d[t0][e], d[t1][e]) * (x, x) -- the
+        // same fp32 FMAs in the same order as the scalar form, half the
+        // instructions (the converted values land in fresh registers anyway)
+        constexpr int CP = (CPT + 1) / 2;
+        float2 dP2[CP][K];
 #pragma unroll
-      for (int t = 0; t < CPT; ++t)
+        for (int t = 0; t < CP; ++t)
 #pragma unroll
-        for (int k = 0; k < K; ++k) dP[t][k] = 0.f;
+          for (int k = 0; k < K; ++k) dP2[t][k] = make_float2(0.f, 0.f);
 #pragma unroll 1
-      for (int v = sub; v < nv; v += kGroup) {
-        float d[CPT][VEC];
+        for (int v = sub; v < nv; v += kGroup) {
+          float d[2 * CP][VEC];
 #pragma unroll
-        for (int t = 0; t < CPT; ++t) {
-          V16<T, VEC> dv;
-          dv.load(dout + b * a.d_b + py[t] * a.d_h + px[t] * a.d_w + v * VEC);
+          for (int t = 0; t < CPT; ++t) {
+            V16<T, VEC> dv;
+            dv.load(dout + b * a.d_b + py[t] * a.d_h + px[t] * a.d_w + v * VEC);
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) d[t][e] = tof(dv.e[e]);
+            for (int e = 0; e < VEC; ++e) d[t][e] = tof(dv.e[e]);
+          }
+          if (CPT % 2 != 0) {
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) d[2 * CP - 1][e] = 0.f;
+          }
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+            V16<T, VEC> vv;
+            vv.load(vb + clampi(cy + a.dy[k], 0, a.H - 1) * a.v_h + clampi(cx + a.dx[k], 0, a.W - 1) * a.v_w +
+                    v * VEC);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) {
+              const float x = tof(vv.e[e]);
+              const float2 xx = make_float2(x, x);
+#pragma unroll
+              for (int t = 0; t < CP; ++t)
+                dP2[t][k] = __ffma2_rn(make_float2(d[2 * t][e], d[2 * t + 1][e]), xx, dP2[t][k]);
+            }
+          }
         }
 #pragma unroll
-        for (int k = 0; k < K; ++k) {
-          V16<T, VEC> vv;
-          vv.load(vb + clampi(cy + a.dy[k], 0, a.H - 1) * a.v_h + clampi(cx + a.dx[k], 0, a.W - 1) * a.v_w + v * VEC);
+        for (int t = 0; t < CPT; ++t)
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) {
-            const float x = tof(vv.e[e]);
+          for (int k = 0; k < K; ++k) dP[t][k] = (t % 2 == 0) ? dP2[t / 2][k].x : dP2[t / 2][k].y;
+      } else {
 #pragma unroll
-            for (int t = 0; t < CPT; ++t) dP[t][k] = fmaf(d[t][e], x, dP[t][k]);
+        for (int t = 0; t < CPT; ++t)
+#pragma unroll
+          for (int k = 0; k < K; ++k) dP[t][k] = 0.f;
+#pragma unroll 1
+        for (int v = sub; v < nv; v += kGroup) {
+          float d[CPT][VEC];
+#pragma unroll
+          for (int t = 0; t < CPT; ++t) {
+            V16<T, VEC> dv;
+            dv.load(dout + b * a.d_b + py[t] * a.d_h + px[t] * a.d_w + v * VEC);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) d[t][e] = tof(dv.e[e]);
+          }
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+            V16<T, VEC> vv;
+            vv.load(vb + clampi(cy + a.dy[k], 0, a.H - 1) * a.v_h + clampi(cx + a.dx[k], 0, a.W - 1) * a.v_w +
+                    v * VEC);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) {
+              const float x = tof(vv.e[e]);
+#pragma unroll
+              for (int t = 0; t < CPT; ++t) dP[t][k] = fmaf(d[t][e], x, dP[t][k]);
+            }
           }
         }
       }
@@ -423,11 +470,27 @@ __global__ void __launch_bounds__(kThreads, 1) dvalue_window_kernel(const Args a
   T* __restrict__ out = static_cast<T*>(a.dvalue) + b * a.dv_b + ny * a.dv_h + v * VEC;
   const int I = IT > 0 ? IT : a.I;
   const bool row_inner = IT > 0 && ny >= PN && ny < a.H - PN;
-  float ring[S][VEC];
+  // accumulators as channel pairs: one packed FMA (pk, pk) * (d[e], d[e+1])
+  // per pair, the same fp32 FMAs as the scalar form
+  constexpr int VP = (VEC + 1) / 2;
+  float2 ring[S][VP];
 #pragma unroll
   for (int s = 0; s < S; ++s)
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) ring[s][e] = 0.f;
+    for (int e = 0; e < VP; ++e) ring[s][e] = make_float2(0.f, 0.f);
+  auto accumulate = [&](float2* acc, float pk, const float* d) {
+    if (VEC % 2 == 0) {
+      const float2 pp = make_float2(pk, pk);
+#pragma unroll
+      for (int e = 0; e < VP; ++e) acc[e] = __ffma2_rn(pp, make_float2(d[2 * e], d[2 * e + 1]), acc[e]);
+    } else {
+      acc[0].x = fmaf(pk, d[0], acc[0].x);
+    }
+  };
+  auto store = [&](T* o, const float2* acc) {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) o[e] = fromf<T>((e % 2 == 0) ? acc[e / 2].x : acc[e / 2].y);
+  };
 
   // ring[slot(dx)] += P_k(child) dout(child) for every dx of offset row i
   auto add_child = [&](auto inner, int i, int cx, int y, int x) {
@@ -443,16 +506,12 @@ __global__ void __launch_bounds__(kThreads, 1) dvalue_window_kernel(const Args a
       if (k < 0) continue;
       const float pk = pp[k];
       if (decltype(inner)::value) {
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) ring[j][e] = fmaf(pk, d[e], ring[j][e]);
+        accumulate(ring[j], pk, d);
       } else {
         const int slot = clampi(cx + j - PN, 0, a.W - 1) - cx + PN;
 #pragma unroll
         for (int q = 0; q < S; ++q)
-          if (q == slot) {
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) ring[q][e] = fmaf(pk, d[e], ring[q][e]);
-          }
+          if (q == slot) accumulate(ring[q], pk, d);
       }
     }
   };
@@ -476,17 +535,13 @@ __global__ void __launch_bounds__(kThreads, 1) dvalue_window_kernel(const Args a
       }
     }
     const int nx = cx - PN;
-    if (nx >= x0) {
-      T* o = out + nx * a.dv_w;
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) o[e] = fromf<T>(ring[0][e]);
-    }
+    if (nx >= x0) store(out + nx * a.dv_w, ring[0]);
 #pragma unroll
     for (int s = 0; s + 1 < S; ++s)
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) ring[s][e] = ring[s + 1][e];
+      for (int e = 0; e < VP; ++e) ring[s][e] = ring[s + 1][e];
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) ring[S - 1][e] = 0.f;
+    for (int e = 0; e < VP; ++e) ring[S - 1][e] = make_float2(0.f, 0.f);
   };
   using Edge = std::integral_constant<bool, false>;
   using Inner = std::integral_constant<bool, true>;
@@ -500,11 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1) dvalue_window_kernel(const Args a
 #pragma unroll
   for (int s = 0; s < S; ++s) {
     const int nx = cend - PN + s;
-    if (nx >= x0 && nx < x1) {
-      T* o = out + nx * a.dv_w;
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) o[e] = fromf<T>(ring[s][e]);
-    }
+    if (nx >= x0 && nx < x1) store(out + nx * a.dv_w, ring[s]);
   }
 }
 
