@@ -126,3 +126,26 @@ def test_gradients_other_factors(I, cuda_lib):
         got = _kernel_grads(*case, K, True, False)
         for name, e, g in zip(("guide", "value", "weight", "bias"), exp, got):
             assert normwise_err(g, e) <= tol, (I, dt, name)
+
+
+@pytest.mark.parametrize("K", [5, 9, 13, 17, 25])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_gradients_tensor_core_dlogit(K, dt, cuda_lib):
+    """16-bit storage, I = 2, C a multiple of 32, even Cg <= 64: dP runs on
+    the tensor cores (tiles of 8 cells; ragged right edge, single rows,
+    one-cell maps).  dW / db are fp32 outputs computed in fp32 from exact
+    products, so they are held to the fp32 bound; dguide / dvalue to the
+    storage type's rounding."""
+    tol_store = 1e-2 if dt == torch.bfloat16 else 2e-3
+    for (B, Cg, C, H, W) in [(2, 64, 32, 5, 11), (1, 16, 64, 1, 3), (1, 8, 96, 3, 8), (1, 2, 32, 2, 1),
+                             (1, 64, 64, 4, 17)]:
+        for conv_res in (True, False):
+            case = list(_case(K, 2, B, Cg, C, H, W, seed=K + C + W, dt=dt, wscale=0.05))
+            case[4] = case[4].to(dt).float()  # the kernel receives dout in the storage type
+            case[2], case[3] = case[2].float(), case[3].float()  # fp32 parameters: fp32 gradients
+            exp = _oracle_grads(*case, K, conv_res, False)
+            got = _kernel_grads(*case, K, conv_res, False)
+            for name, e, g, tol in zip(("guide", "value", "weight", "bias"), exp, got,
+                                       (tol_store, tol_store, 1e-4, 1e-4)):
+                err = normwise_err(g, e)
+                assert err <= tol, (K, dt, B, Cg, C, H, W, conv_res, name, err)

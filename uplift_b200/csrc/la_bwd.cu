@@ -559,7 +559,306 @@ __global__ void __launch_bounds__(kThreads, 1) dvalue_window_kernel(const Args a
   }
 }
 
+// ---------------------------------------------------------------------------
+// dlogit on tensor cores (16-bit storage, I = 2, C % 32 == 0, even Cg <= 64,
+// offsets within +-PN, PN <= 2).  A warp owns a tile of 8 cells of one cell
+// row = 32 output pixels (two rows of 16 children).  For each offset row
+// dy, dP over the tile is one small GEMM
+//   D_dy[16 px x 16 window columns] = dout[16 px x C] . V_dy[16 x C]^T
+// (window column j = value pixel clamp(cx0 - PN + j) of row clamp(cy + dy)),
+// run as mma.sync m16n8k16 with fp32 accumulation: products of 16-bit
+// values are exact, so only the summation order differs from the CUDA-core
+// kernel.  Operand fragments come straight from global memory as 16-byte
+// vectors: thread (g = lane / 4, t = lane % 4) loads channels [8t, 8t + 8)
+// of a 32-channel chunk for its A rows (pixels g, g + 8) and its B column
+// (window column g); the k-step s of the chunk takes channel pairs 4s and
+// 4s + 2 of that vector for the fragment's low and high k halves -- one
+// permutation of the channels applied to A and B alike, so the dot products
+// are unchanged.  D is staged in shared memory; then a lane per pixel picks
+// dP_k = D_dy(k)[pixel][cell + dx(k) + PN] and forms dl (fp32, as the
+// CUDA-core kernel); then a lane per guide-channel pair forms dguide and
+// accumulates dW / db over all of the warp's tiles in registers.
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+__device__ __forceinline__ uint32_t word(const uint4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
+constexpr int kMmaWarps = 4;   // warps per dlogit_mma CTA
+constexpr int kMmaDRow = 20;   // floats per staged D row (16 columns + pad)
+constexpr int kMmaStages = 3;  // 32-channel chunks in flight per thread
+
+template <int K>
+__host__ __device__ constexpr int kpad4() { return (K + 3) & ~3; }
+
+// 16-byte vectors a thread loads per chunk: 2 x 2 A rows, 2 B columns per dy
+template <int PN>
+__host__ __device__ constexpr int mma_vecs() { return 4 + 2 * (2 * PN + 1); }
+
+// per-warp shared floats: the chunk ring, reused after the GEMM for the
+// staged D (2 x (2 PN + 1) x 16 rows) and dl (32 x KP)
+template <int K, int PN>
+__host__ __device__ constexpr int mma_warp_floats() {
+  return kMmaStages * mma_vecs<PN>() * 32 * 4 > 2 * (2 * PN + 1) * 16 * kMmaDRow + 32 * kpad4<K>()
+             ? kMmaStages * mma_vecs<PN>() * 32 * 4
+             : 2 * (2 * PN + 1) * 16 * kMmaDRow + 32 * kpad4<K>();
+}
+
+// shared floats: dW [K][Cg] and db [K] (each rounded up to 4 floats), W'
+// channel pairs [K][32 lanes] (float2), then the warps' regions
+template <int K, int PN>
+__host__ __device__ constexpr size_t mma_smem_floats(int Cg) {
+  return (size_t)((K * Cg + 3) & ~3) + kpad4<K>() + (size_t)K * 64 + (size_t)kMmaWarps * mma_warp_floats<K, PN>();
+}
+
+__device__ __forceinline__ void bwd_cp_async16(void* dst_smem, const void* src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst_smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void bwd_cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bwd_cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+template <typename T, int K, int PN>
+__global__ void __launch_bounds__(kMmaWarps * 32, 2) dlogit_mma_kernel(const Args a) {
+  constexpr int S = 2 * PN + 1;
+  constexpr int KP = kpad4<K>();
+  constexpr int kWarpFloats = mma_warp_floats<K, PN>();
+  constexpr int NV = mma_vecs<PN>();
+  using T2 = typename std::conditional<std::is_same<T, __nv_bfloat16>::value, __nv_bfloat162, __half2>::type;
+  extern __shared__ __align__(16) float smem[];
+  float* s_dw = smem;                                  // [K][Cg]
+  float* s_db = s_dw + ((K * a.Cg + 3) & ~3);          // [K]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float2* s_wp = reinterpret_cast<float2*>(s_db + KP);  // [K][32]: W' of channel pair `lane`
+  float* s_D = s_db + KP + K * 64 + warp * kWarpFloats;  // [2][S][16][kMmaDRow]
+  float* s_L = s_D + 2 * S * 16 * kMmaDRow;            // [32][KP]
+  uint4* ring = reinterpret_cast<uint4*>(s_D) + lane;  // [kMmaStages][NV][32 lanes], this lane's column
+  for (int i = threadIdx.x; i < ((K * a.Cg + 3) & ~3) + KP; i += kMmaWarps * 32) smem[i] = 0.f;
+  for (int i = threadIdx.x; i < K * 32; i += kMmaWarps * 32) {
+    const int k = i / 32, cp = 2 * (i % 32);
+    s_wp[i] = cp < a.Cg ? make_float2(a.weight[(size_t)k * a.Cg + cp] + ((a.conv_res && k == cp) ? 1.f : 0.f),
+                                      a.weight[(size_t)k * a.Cg + cp + 1] + ((a.conv_res && k == cp + 1) ? 1.f : 0.f))
+                        : make_float2(0.f, 0.f);
+  }
+  __syncthreads();
+
+  const T* __restrict__ dout = static_cast<const T*>(a.dout);
+  const T* __restrict__ guide = static_cast<const T*>(a.guide);
+  const T* __restrict__ value = static_cast<const T*>(a.value);
+  const int g = lane >> 2, t4 = lane & 3;
+  const bool params = a.dweight != nullptr || a.dbias != nullptr;
+  // guide-channel pair of this lane in the dguide / dW phase
+  const int c2 = 2 * lane;
+  const bool has_pair = c2 < a.Cg;
+  float2 wacc[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) wacc[k] = make_float2(0.f, 0.f);
+  float bacc = 0.f;  // db[lane] for lane < K
+
+  const int tw = (a.W + 7) / 8;
+  const int64_t ntiles = (int64_t)a.B * a.H * tw;
+  for (int64_t tile = (int64_t)blockIdx.x * kMmaWarps + warp; tile < ntiles;
+       tile += (int64_t)gridDim.x * kMmaWarps) {
+    const int tx = (int)(tile % tw);
+    const int64_t rr = tile / tw;
+    const int cy = (int)(rr % a.H), b = (int)(rr / a.H);
+    const int cx0 = tx * 8;
+    const T* db = dout + b * a.d_b;
+    const T* vb = value + b * a.v_b;
+
+    // ---- D_dy = dout_tile . V_window^T for every dy
+    float acc[2][S][2][4];
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+      for (int i = 0; i < S; ++i)
+#pragma unroll
+        for (int ni = 0; ni < 2; ++ni)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[mi][i][ni][q] = 0.f;
+    int64_t aoff[2][2];
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        aoff[mi][h] = (int64_t)(2 * cy + mi) * a.d_h + (int64_t)min(2 * cx0 + g + 8 * h, a.Wo - 1) * a.d_w + 8 * t4;
+    int64_t bcol[2];
+#pragma unroll
+    for (int ni = 0; ni < 2; ++ni) bcol[ni] = (int64_t)clampi(cx0 - PN + 8 * ni + g, 0, a.W - 1) * a.v_w + 8 * t4;
+    // chunk ring: each thread copies its own 16-byte vectors (A rows, B
+    // columns per dy) kMmaStages - 1 chunks ahead and reads back only those,
+    // so no other thread is waited for
+    auto issue = [&](int chunk) {
+      const int c0 = chunk * 32;
+      uint4* dst = ring + (chunk % kMmaStages) * NV * 32;
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) bwd_cp_async16(dst + (2 * mi + h) * 32, db + aoff[mi][h] + c0);
+#pragma unroll
+      for (int i = 0; i < S; ++i) {
+        const int64_t brow = (int64_t)clampi(cy + i - PN, 0, a.H - 1) * a.v_h + c0;
+#pragma unroll
+        for (int ni = 0; ni < 2; ++ni) bwd_cp_async16(dst + (4 + 2 * i + ni) * 32, vb + brow + bcol[ni]);
+      }
+    };
+    const int nch = a.C / 32;
+#pragma unroll
+    for (int q = 0; q < kMmaStages - 1; ++q) {
+      if (q < nch) issue(q);
+      bwd_cp_async_commit();
+    }
+#pragma unroll 1
+    for (int ch = 0; ch < nch; ++ch) {
+      bwd_cp_async_wait<kMmaStages - 2>();  // chunk ch has landed
+      if (ch + kMmaStages - 1 < nch) issue(ch + kMmaStages - 1);  // into the slot chunk ch - 1 used
+      bwd_cp_async_commit();
+      const uint4* src = ring + (ch % kMmaStages) * NV * 32;
+      uint4 av[2][2];
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) av[mi][h] = src[(2 * mi + h) * 32];
+#pragma unroll
+      for (int i = 0; i < S; ++i) {
+        uint4 bv[2];
+#pragma unroll
+        for (int ni = 0; ni < 2; ++ni) bv[ni] = src[(4 + 2 * i + ni) * 32];
+#pragma unroll
+        for (int s = 0; s < 2; ++s)
+#pragma unroll
+          for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+            for (int ni = 0; ni < 2; ++ni)
+              mma16816<T>(acc[mi][i][ni], word(av[mi][0], 2 * s), word(av[mi][1], 2 * s), word(av[mi][0], 2 * s + 1),
+                          word(av[mi][1], 2 * s + 1), word(bv[ni], 2 * s), word(bv[ni], 2 * s + 1));
+      }
+    }
+    bwd_cp_async_wait<0>();
+    __syncwarp();  // the ring area is rewritten as D below
+    // stage D: thread holds rows g, g + 8 and columns 8 ni + 2 t4 + {0, 1}
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+      for (int i = 0; i < S; ++i)
+#pragma unroll
+        for (int ni = 0; ni < 2; ++ni) {
+          float* row = s_D + ((mi * S + i) * 16 + g) * kMmaDRow + 8 * ni + 2 * t4;
+          *reinterpret_cast<float2*>(row) = make_float2(acc[mi][i][ni][0], acc[mi][i][ni][1]);
+          *reinterpret_cast<float2*>(row + 8 * kMmaDRow) = make_float2(acc[mi][i][ni][2], acc[mi][i][ni][3]);
+        }
+    __syncwarp();
+
+    // ---- softmax backward, a lane per pixel (pixel = lane: child row
+    // lane / 16, child column lane % 16 of the tile)
+    {
+      const int mi = lane >> 4, m = lane & 15, c = m >> 1;
+      const bool valid = cx0 + c < a.W;
+      const int x = min(2 * cx0 + m, a.Wo - 1), y = 2 * cy + mi;
+      const float* pp = a.probs + (((int64_t)b * a.Ho + y) * a.Wo + x) * K;
+      float pk[K], dP[K];
+      float sdot = 0.f;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        pk[k] = pp[k];
+        dP[k] = s_D[((mi * S + a.dy[k] + PN) * 16 + m) * kMmaDRow + c + a.dx[k] + PN];
+        sdot = fmaf(pk[k], dP[k], sdot);
+      }
+      float dlv[KP];
+#pragma unroll
+      for (int k = 0; k < KP; ++k) {
+        const int kk = k < K ? k : K - 1;
+        dlv[k] = (k < K && valid) ? pk[kk] * (dP[kk] - sdot) : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < KP; k += 4)
+        *reinterpret_cast<float4*>(s_L + lane * KP + k) = make_float4(dlv[k], dlv[k + 1], dlv[k + 2], dlv[k + 3]);
+    }
+    __syncwarp();
+
+    // ---- dguide, dW, db: a lane per guide-channel pair, over the 32 pixels
+    // (in two halves of 16 pixels, the guide pairs of a half loaded up front:
+    // one latency per half)
+    float2 wp[K];  // W' of this lane's channel pair
+#pragma unroll
+    for (int k = 0; k < K; ++k) wp[k] = s_wp[k * 32 + lane];
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      T2 gpre[16];
+      if (params && has_pair) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const int x = min(2 * cx0 + q, a.Wo - 1), y = 2 * cy + half;
+          gpre[q] = *reinterpret_cast<const T2*>(guide + b * a.g_b + (int64_t)y * a.g_h + (int64_t)x * a.g_w + c2);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const int p = 16 * half + q;
+        if (cx0 + (q >> 1) >= a.W) continue;  // warp-uniform
+        const int x = 2 * cx0 + q, y = 2 * cy + half;
+        float dl[KP];
+#pragma unroll
+        for (int k = 0; k < KP; k += 4) {
+          const float4 v4 = *reinterpret_cast<const float4*>(s_L + p * KP + k);
+          dl[k] = v4.x; dl[k + 1] = v4.y; dl[k + 2] = v4.z; dl[k + 3] = v4.w;
+        }
+        if (has_pair) {
+          if (a.dguide != nullptr) {
+            float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < K; ++k) s2 = __ffma2_rn(make_float2(dl[k], dl[k]), wp[k], s2);
+            T2 o2;
+            o2.x = fromf<T>(s2.x);
+            o2.y = fromf<T>(s2.y);
+            *reinterpret_cast<T2*>(static_cast<T*>(a.dguide) + b * a.dg_b + (int64_t)y * a.dg_h +
+                                   (int64_t)x * a.dg_w + c2) = o2;
+          }
+          if (params) {
+            const float2 g2 = make_float2(__low2float(gpre[q]), __high2float(gpre[q]));
+#pragma unroll
+            for (int k = 0; k < K; ++k) wacc[k] = __ffma2_rn(make_float2(dl[k], dl[k]), g2, wacc[k]);
+          }
+        }
+        if (params && lane < K) bacc += s_L[p * KP + lane];
+      }
+    }
+    __syncwarp();  // s_D / s_L are rewritten by the next tile
+  }
+  if (!params) return;
+  if (has_pair) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      atomicAdd(s_dw + k * a.Cg + c2, wacc[k].x);
+      atomicAdd(s_dw + k * a.Cg + c2 + 1, wacc[k].y);
+    }
+  }
+  if (lane < K) atomicAdd(s_db + lane, bacc);
+  __syncthreads();
+  for (int i = threadIdx.x; i < K * a.Cg; i += kMmaWarps * 32)
+    if (a.dweight != nullptr) atomicAdd(a.dweight + i, s_dw[i]);
+  if (a.dbias != nullptr && threadIdx.x < K) atomicAdd(a.dbias + threadIdx.x, s_db[threadIdx.x]);
+}
+
 struct Plan {
+  int mma_pn;    // 1 or 2: tensor-core dlogit (dlogit_mma_kernel<PN>); 0: CUDA-core dlogit
   int window;    // 1: sliding-window dV (reference offset table); 0: general dV kernel
   int seg_len;   // value columns per window thread
   int nseg;
@@ -583,7 +882,25 @@ int launch_cv(const Args& a, const Plan& plan, cudaStream_t stream) {
   if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   const int64_t pblocks = std::min<int64_t>((npix + kThreads - 1) / kThreads, (int64_t)sms * 16);
   probs_kernel<T, K, GV><<<(unsigned)pblocks, kThreads, smem_p, stream>>>(a);
-  if (a.dguide != nullptr || a.dweight != nullptr || a.dbias != nullptr) {
+  bool dlogit_done = false;
+  if constexpr (sizeof(T) == 2) {
+    if (plan.mma_pn > 0 && (a.dguide != nullptr || a.dweight != nullptr || a.dbias != nullptr)) {
+      auto kern = plan.mma_pn == 1 ? dlogit_mma_kernel<T, K, 1> : dlogit_mma_kernel<T, K, 2>;
+      const size_t smem_m =
+          sizeof(float) * (plan.mma_pn == 1 ? mma_smem_floats<K, 1>(a.Cg) : mma_smem_floats<K, 2>(a.Cg));
+      if (smem_m > (size_t)optin) return fail(UPLIFT_LA_ERR_SHAPE, "backward: tensor-core dlogit smem");
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_m);
+      if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      int occ = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kMmaWarps * 32, smem_m) != cudaSuccess || occ < 1)
+        occ = 1;
+      const int64_t tiles = (int64_t)a.B * a.H * ((a.W + 7) / 8);
+      const int64_t mblocks = std::min<int64_t>((tiles + kMmaWarps - 1) / kMmaWarps, (int64_t)sms * occ);
+      kern<<<(unsigned)mblocks, kMmaWarps * 32, smem_m, stream>>>(a);
+      dlogit_done = true;
+    }
+  }
+  if (!dlogit_done && (a.dguide != nullptr || a.dweight != nullptr || a.dbias != nullptr)) {
     int occ = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, dlogit_kernel<T, K, CPT, VEC>, kDThreads, smem_d) !=
             cudaSuccess || occ < 1)
@@ -721,7 +1038,24 @@ extern "C" int uplift_la_backward(const void* dout, const int64_t dout_strides[4
   const bool gvec = Cg % ve == 0 && a16(guide) && a.g_b % ve == 0 && a.g_h % ve == 0 && a.g_w % ve == 0;
   // sliding-window dV when the offsets are the reference's table for K; row
   // segments sized so that about 2048 threads per SM are busy
-  bwd::Plan plan{0, W, 1};
+  bwd::Plan plan{0, 0, W, 1};
+  {
+    // tensor-core dlogit: 16-bit storage, I = 2, C % 32 == 0, even Cg <= 64,
+    // 16-byte dout / value rows, 4-byte guide / dguide channel pairs,
+    // offsets within +-2, softmax (hardmax has no logit gradient);
+    // ULA_BWD_MMA=0 selects the CUDA-core dlogit instead (comparisons)
+    int maxd = 0;
+    for (int k = 0; k < K; ++k) maxd = std::max(maxd, std::max(std::abs((int)a.dy[k]), std::abs((int)a.dx[k])));
+    auto a4 = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 3u) == 0; };
+    bool ok = dtype != UPLIFT_LA_F32 && I == 2 && C % 32 == 0 && vec && Cg % 2 == 0 && Cg <= 64 && !hardmax &&
+              maxd <= 2 && a4(guide) && a.g_b % 2 == 0 && a.g_h % 2 == 0 && a.g_w % 2 == 0;
+    if (dguide != nullptr) ok = ok && a4(dguide) && a.dg_b % 2 == 0 && a.dg_h % 2 == 0 && a.dg_w % 2 == 0;
+    static const bool mma_env = [] {
+      const char* e = getenv("ULA_BWD_MMA");
+      return e == nullptr || atoi(e) != 0;
+    }();
+    if (ok && mma_env) plan.mma_pn = maxd < 1 ? 1 : maxd;
+  }
   bool canonical = true;
   for (int k = 0; k < K; ++k) {
     int kk = -1;
