@@ -75,16 +75,20 @@ extern "C" int uplift_la_backward(const void* dout, const int64_t dout_strides[4
   // segments sized so that about 2048 threads per SM are busy
   bwd::Plan plan{0, 0, W, 1};
   {
-    // tensor-core dlogit: 16-bit storage, I = 2, C % 32 == 0, even Cg <= 64,
-    // 16-byte dout / value rows, 4-byte guide / dguide channel pairs,
-    // offsets within +-2, softmax (hardmax has no logit gradient);
+    // tensor-core dlogit: I = 2, even Cg <= 64, C % 32 == 0 (16-bit storage)
+    // or C % 16 == 0 (fp32), 16-byte dout / value rows, aligned guide / dguide
+    // channel pairs, offsets within +-2, softmax (hardmax has no logit gradient);
     // ULA_BWD_MMA=0 selects the CUDA-core dlogit instead (comparisons)
     int maxd = 0;
     for (int k = 0; k < K; ++k) maxd = std::max(maxd, std::max(std::abs((int)a.dy[k]), std::abs((int)a.dx[k])));
-    auto a4 = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 3u) == 0; };
-    bool ok = dtype != UPLIFT_LA_F32 && I == 2 && C % 32 == 0 && vec && Cg % 2 == 0 && Cg <= 64 && !hardmax &&
-              maxd <= 2 && a4(guide) && a.g_b % 2 == 0 && a.g_h % 2 == 0 && a.g_w % 2 == 0;
-    if (dguide != nullptr) ok = ok && a4(dguide) && a.dg_b % 2 == 0 && a.dg_h % 2 == 0 && a.dg_w % 2 == 0;
+    // (fp32: C % 16 == 0 and 8-byte guide pairs)
+    const unsigned pair_align = dtype == UPLIFT_LA_F32 ? 7u : 3u;
+    auto ap = [pair_align](const void* q) {
+      return q == nullptr || (reinterpret_cast<uintptr_t>(q) & pair_align) == 0;
+    };
+    bool ok = I == 2 && C % (dtype == UPLIFT_LA_F32 ? 16 : 32) == 0 && vec && Cg % 2 == 0 && Cg <= 64 &&
+              !hardmax && maxd <= 2 && ap(guide) && a.g_b % 2 == 0 && a.g_h % 2 == 0 && a.g_w % 2 == 0;
+    if (dguide != nullptr) ok = ok && ap(dguide) && a.dg_b % 2 == 0 && a.dg_h % 2 == 0 && a.dg_w % 2 == 0;
     static const bool mma_env = [] {
       const char* e = getenv("ULA_BWD_MMA");
       return e == nullptr || atoi(e) != 0;

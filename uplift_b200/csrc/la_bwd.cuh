@@ -563,8 +563,8 @@ __global__ void __launch_bounds__(kThreads, 1) dvalue_window_kernel(const Args a
 }
 
 // ---------------------------------------------------------------------------
-// dlogit on tensor cores (16-bit storage, I = 2, C % 32 == 0, even Cg <= 64,
-// offsets within +-PN, PN <= 2).  A warp owns a tile of 8 cells of one cell
+// dlogit on tensor cores (I = 2, even Cg <= 64, offsets within +-PN, PN <= 2;
+// 16-bit storage with C % 32 == 0, or fp32 with C % 16 == 0).  A warp owns a tile of 8 cells of one cell
 // row = 32 output pixels (two rows of 16 children).  For each offset row
 // dy, dP over the tile is one small GEMM
 //   D_dy[16 px x 16 window columns] = dout[16 px x C] . V_dy[16 x C]^T
@@ -577,7 +577,10 @@ __global__ void __launch_bounds__(kThreads, 1) dvalue_window_kernel(const Args a
 // (window column g); the k-step s of the chunk takes channel pairs 4s and
 // 4s + 2 of that vector for the fragment's low and high k halves -- one
 // permutation of the channels applied to A and B alike, so the dot products
-// are unchanged.  D is staged in shared memory; then a lane per pixel picks
+// are unchanged.  fp32 storage: 16-channel chunks, channels [4t, 4t + 4) per
+// thread, each operand pair split into bf16 hi + lo and multiplied as
+// hi*hi + hi*lo + lo*hi (about 2^-16 relative per product, the split the
+// wide-guide forward kernel uses).  D is staged in shared memory; then a lane per pixel picks
 // dP_k = D_dy(k)[pixel][cell + dx(k) + PN] and forms dl (fp32, as the
 // CUDA-core kernel); then a lane per guide-channel pair forms dguide and
 // accumulates dW / db over all of the warp's tiles in registers.
@@ -602,6 +605,22 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 __device__ __forceinline__ uint32_t word(const uint4& v, int i) {
   return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
+
+// fp32 pair (two 32-bit words) -> bf16x2 high part and bf16x2 remainder:
+// x = hi + lo to about 2^-16 relative, so hi*hi + hi*lo + lo*hi is an fp32
+// product to that accuracy (the dropped lo*lo term is ~2^-16 smaller).
+__device__ __forceinline__ void split_bf16x2(uint32_t xa, uint32_t xb, uint32_t& hi, uint32_t& lo) {
+  const float a = __uint_as_float(xa), b = __uint_as_float(xb);
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const float2 hf = __bfloat1622float2(h);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+__device__ __forceinline__ float2 pair_to_float2(float2 v) { return v; }
+__device__ __forceinline__ float2 pair_to_float2(__nv_bfloat162 v) { return __bfloat1622float2(v); }
+__device__ __forceinline__ float2 pair_to_float2(__half2 v) { return __half22float2(v); }
 
 constexpr int kMmaWarps = 4;   // warps per dlogit_mma CTA
 constexpr int kMmaDRow = 20;   // floats per staged D row (16 columns + pad)
@@ -644,7 +663,15 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) dlogit_mma_kernel(const Arg
   constexpr int KP = kpad4<K>();
   constexpr int kWarpFloats = mma_warp_floats<K, PN>();
   constexpr int NV = mma_vecs<PN>();
-  using T2 = typename std::conditional<std::is_same<T, __nv_bfloat16>::value, __nv_bfloat162, __half2>::type;
+  using T2 = typename std::conditional<
+      std::is_same<T, __nv_bfloat16>::value, __nv_bfloat162,
+      typename std::conditional<std::is_same<T, __half>::value, __half2, float2>::type>::type;
+  // fp32 storage: 16-channel chunks (one k-step; a thread's 16-byte vector
+  // holds channels [4t, 4t + 4)), each operand split into bf16 hi + lo and
+  // multiplied with three MMAs; 16-bit storage: 32-channel chunks (two
+  // k-steps; channels [8t, 8t + 8)), one MMA each
+  constexpr bool kF32 = std::is_same<T, float>::value;
+  constexpr int CH = kF32 ? 16 : 32;
   extern __shared__ __align__(16) float smem[];
   float* s_dw = smem;                                  // [K][Cg]
   float* s_db = s_dw + ((K * a.Cg + 3) & ~3);          // [K]
@@ -701,15 +728,15 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) dlogit_mma_kernel(const Arg
     for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
       for (int h = 0; h < 2; ++h)
-        aoff[mi][h] = (int64_t)(2 * cy + mi) * a.d_h + (int64_t)min(2 * cx0 + g + 8 * h, a.Wo - 1) * a.d_w + 8 * t4;
+        aoff[mi][h] = (int64_t)(2 * cy + mi) * a.d_h + (int64_t)min(2 * cx0 + g + 8 * h, a.Wo - 1) * a.d_w + (CH / 4) * t4;
     int64_t bcol[2];
 #pragma unroll
-    for (int ni = 0; ni < 2; ++ni) bcol[ni] = (int64_t)clampi(cx0 - PN + 8 * ni + g, 0, a.W - 1) * a.v_w + 8 * t4;
+    for (int ni = 0; ni < 2; ++ni) bcol[ni] = (int64_t)clampi(cx0 - PN + 8 * ni + g, 0, a.W - 1) * a.v_w + (CH / 4) * t4;
     // chunk ring: each thread copies its own 16-byte vectors (A rows, B
     // columns per dy) kMmaStages - 1 chunks ahead and reads back only those,
     // so no other thread is waited for
     auto issue = [&](int chunk) {
-      const int c0 = chunk * 32;
+      const int c0 = chunk * CH;
       uint4* dst = ring + (chunk % kMmaStages) * NV * 32;
 #pragma unroll
       for (int mi = 0; mi < 2; ++mi)
@@ -722,7 +749,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) dlogit_mma_kernel(const Arg
         for (int ni = 0; ni < 2; ++ni) bwd_cp_async16(dst + (4 + 2 * i + ni) * 32, vb + brow + bcol[ni]);
       }
     };
-    const int nch = a.C / 32;
+    const int nch = a.C / CH;
 #pragma unroll
     for (int q = 0; q < kMmaStages - 1; ++q) {
       if (q < nch) issue(q);
@@ -744,14 +771,42 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) dlogit_mma_kernel(const Arg
         uint4 bv[2];
 #pragma unroll
         for (int ni = 0; ni < 2; ++ni) bv[ni] = src[(4 + 2 * i + ni) * 32];
-#pragma unroll
-        for (int s = 0; s < 2; ++s)
+        if constexpr (kF32) {
+          // words 0, 1 = channels 4t, 4t + 1 (low k half), words 2, 3 = 4t + 2, 4t + 3
+          uint32_t ah[2][2][2], al[2][2][2], bh[2][2], bl[2][2];
 #pragma unroll
           for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-            for (int ni = 0; ni < 2; ++ni)
-              mma16816<T>(acc[mi][i][ni], word(av[mi][0], 2 * s), word(av[mi][1], 2 * s), word(av[mi][0], 2 * s + 1),
-                          word(av[mi][1], 2 * s + 1), word(bv[ni], 2 * s), word(bv[ni], 2 * s + 1));
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int q = 0; q < 2; ++q)
+                split_bf16x2(word(av[mi][h], 2 * q), word(av[mi][h], 2 * q + 1), ah[mi][h][q], al[mi][h][q]);
+#pragma unroll
+          for (int ni = 0; ni < 2; ++ni)
+#pragma unroll
+            for (int q = 0; q < 2; ++q) split_bf16x2(word(bv[ni], 2 * q), word(bv[ni], 2 * q + 1), bh[ni][q], bl[ni][q]);
+#pragma unroll
+          for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+            for (int ni = 0; ni < 2; ++ni) {
+              mma16816<__nv_bfloat16>(acc[mi][i][ni], ah[mi][0][0], ah[mi][1][0], ah[mi][0][1], ah[mi][1][1],
+                                      bh[ni][0], bh[ni][1]);
+              mma16816<__nv_bfloat16>(acc[mi][i][ni], ah[mi][0][0], ah[mi][1][0], ah[mi][0][1], ah[mi][1][1],
+                                      bl[ni][0], bl[ni][1]);
+              mma16816<__nv_bfloat16>(acc[mi][i][ni], al[mi][0][0], al[mi][1][0], al[mi][0][1], al[mi][1][1],
+                                      bh[ni][0], bh[ni][1]);
+            }
+        } else {
+#pragma unroll
+          for (int s = 0; s < 2; ++s)
+#pragma unroll
+            for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+              for (int ni = 0; ni < 2; ++ni)
+                mma16816<T>(acc[mi][i][ni], word(av[mi][0], 2 * s), word(av[mi][1], 2 * s),
+                            word(av[mi][0], 2 * s + 1), word(av[mi][1], 2 * s + 1), word(bv[ni], 2 * s),
+                            word(bv[ni], 2 * s + 1));
+        }
       }
     }
     bwd_cp_async_wait<0>();
@@ -835,7 +890,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) dlogit_mma_kernel(const Arg
                                    (int64_t)x * a.dg_w + c2) = o2;
           }
           if (params) {
-            const float2 g2 = make_float2(__low2float(gpre[q]), __high2float(gpre[q]));
+            const float2 g2 = pair_to_float2(gpre[q]);
 #pragma unroll
             for (int k = 0; k < K; ++k) wacc[k] = __ffma2_rn(make_float2(dl[k], dl[k]), g2, wacc[k]);
           }
@@ -886,7 +941,7 @@ int launch_cv(const Args& a, const Plan& plan, cudaStream_t stream) {
   const int64_t pblocks = std::min<int64_t>((npix + kThreads - 1) / kThreads, (int64_t)sms * 16);
   probs_kernel<T, K, GV><<<(unsigned)pblocks, kThreads, smem_p, stream>>>(a);
   bool dlogit_done = false;
-  if constexpr (sizeof(T) == 2) {
+  {
     if (plan.mma_pn > 0 && (a.dguide != nullptr || a.dweight != nullptr || a.dbias != nullptr)) {
       auto kern = plan.mma_pn == 1 ? dlogit_mma_kernel<T, K, 1> : dlogit_mma_kernel<T, K, 2>;
       const size_t smem_m =
