@@ -149,3 +149,28 @@ def test_gradients_tensor_core_dlogit(K, dt, cuda_lib):
                                        (tol_store, tol_store, 1e-4, 1e-4)):
                 err = normwise_err(g, e)
                 assert err <= tol, (K, dt, B, Cg, C, H, W, conv_res, name, err)
+
+
+@pytest.mark.parametrize("K", [5, 9, 13, 17, 25])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_gradients_value_wide_channels(K, dt, cuda_lib):
+    """dV of 16-bit storage with 128-256 channels: ragged row ends, single
+    rows, clamped edges, the reference's and a permuted offset table (the
+    sliding-window and the general dV kernel), hardmax."""
+    tol_store = 1e-2 if dt == torch.bfloat16 else 2e-3
+    offsets, pn = neighbourhood(K)
+    perm = torch.randperm(K, generator=torch.Generator().manual_seed(7 * K)).tolist()
+    for table in (offsets, [offsets[i] for i in perm]):
+        for (B, Cg, C, H, W, hardmax) in [(2, 16, 128, 5, 19, False), (1, 8, 256, 1, 3, False),
+                                          (1, 64, 128, 4, 33, False), (1, 16, 128, 3, 7, True)]:
+            case = list(_case(K, 2, B, Cg, C, H, W, seed=K + C + W, dt=dt, wscale=0.05))
+            case[4] = case[4].to(dt).float()
+            case[2], case[3] = case[2].float(), case[3].float()
+            ts = [t.double().requires_grad_() for t in case[:4]]
+            out = lao.local_attender(*ts, hardmax=hardmax, offsets=table, pn=pn)
+            (out * case[4].double()).sum().backward()
+            tg = [t.to(DEV).requires_grad_() for t in case[:4]]
+            o = ops.local_attender(*tg, table, pn, hardmax=hardmax)
+            (o.float() * case[4].to(DEV)).sum().backward()
+            err = normwise_err(tg[1].grad.float().cpu(), ts[1].grad)
+            assert err <= tol_store, (K, dt, B, Cg, C, H, W, hardmax, err)
