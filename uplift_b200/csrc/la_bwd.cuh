@@ -17,7 +17,8 @@
 // fp32 workspace [B, Ho, Wo, K] (probs_kernel, a thread per pixel);
 // dlogit forms dP, dl and dg and reduces dW / db over the CTA in shared
 // memory before one global atomic add per entry -- dlogit_mma_kernel (dP on
-// the tensor cores, 16-bit storage) or dlogit_kernel (a group of 8 lanes per
+// the tensor cores; fp32 through a bf16 hi / lo split) or dlogit_kernel
+// (other shapes: a group of 8 lanes per
 // unit of CPT children of one cell, lanes over 16-byte channel vectors, so
 // each dout row and each neighbour value row is read once per unit); and
 // dvalue_window_kernel gathers dV with a sliding window: a thread owns one
@@ -564,8 +565,9 @@ __global__ void __launch_bounds__(kThreads, 1) dvalue_window_kernel(const Args a
 
 // ---------------------------------------------------------------------------
 // dlogit on tensor cores (I = 2, even Cg <= 64, offsets within +-PN, PN <= 2;
-// 16-bit storage with C % 32 == 0, or fp32 with C % 16 == 0).  A warp owns a tile of 8 cells of one cell
-// row = 32 output pixels (two rows of 16 children).  For each offset row
+// 16-bit storage with C % 32 == 0, or fp32 with C % 16 == 0).  A warp owns a
+// tile of 8 cells of one cell row = 32 output pixels (two rows of 16
+// children).  For each offset row
 // dy, dP over the tile is one small GEMM
 //   D_dy[16 px x 16 window columns] = dout[16 px x C] . V_dy[16 x C]^T
 // (window column j = value pixel clamp(cx0 - PN + j) of row clamp(cy + dy)),
