@@ -132,9 +132,13 @@ int uplift_la_backward(const void* dout, const int64_t dout_strides[4],
  * The workspace is a fixed array of UPLIFT_LA_NOALLOC_MAX_PROBS floats
  * (32 MiB) inside the library, which every GPU that loads the library
  * holds until the process exits.  Calls with B*(I*H)*(I*W)*K above that
- * maximum fail with UPLIFT_LA_ERR_SHAPE and launch nothing.  The first call
- * on a device looks the array's device address up (cudaGetSymbolAddress):
- * make that first call before any stream capture.  All calls share the one
+ * maximum fail with UPLIFT_LA_ERR_SHAPE and launch nothing (other invalid
+ * arguments are reported first, as by uplift_la_backward).  The first call
+ * on a device looks the array's device address up (cudaGetSymbolAddress)
+ * and keeps it for later calls: make that first call before any stream
+ * capture.  The kept address belongs to the device's primary context (the
+ * runtime's default); after cudaDeviceReset it is stale, so do not use this
+ * entry point again in that process.  All calls share the one
  * array: calls whose kernels overlap on the GPU (other streams, other host
  * threads) race on it, so serialise them.  Every call rewrites the part it
  * reads; dweight / dbias still accumulate into the caller's zeroed outputs.
@@ -178,6 +182,18 @@ int uplift_la_last_kernel(void);
  * split, 4 epilogue) whose bounded wait expired first.  Synchronises with
  * the device; `clear` resets the word.  Returns -1 if the read failed. */
 int uplift_la_device_status(int clear);
+
+/* Registers a host-visible copy of the device status word: `word` points to
+ * 4 bytes of pinned host memory that the device can address (cudaHostAlloc
+ * memory under unified addressing; NULL unregisters).  Every later
+ * tensor-core launch also writes the failing role's code there when a
+ * bounded wait expires, so the host can poll a plain memory read -- no
+ * synchronisation, no device call -- and learn that a finished launch left
+ * its output incomplete.  The library never clears the word; the caller does.
+ * The word must stay allocated while launches that received it can run.
+ * Process-wide, all devices.  No reference counterpart (the reference's
+ * Triton kernels have no waits that can expire). */
+int uplift_la_set_host_status_word(unsigned int* word);
 
 /* Testing only: fault = 1 makes the tensor-core kernels' guide producers issue
  * no loads, so the consumers' bounded waits run out; wait_limit_ns (0 =

@@ -133,10 +133,47 @@ def test_expired_wait_is_reported_and_context_survives(cuda_lib):
     try:
         _run(_native.POLICY_TENSOR_CORE, guide, value, weight, bias, 17)  # synchronises
         status = _native.device_status(clear=True)
+        host_word = _native.host_status.value()
+        _native.host_status.clear()  # this test reads the device copy itself
     finally:
         lib.uplift_la_test_hook(0, 0)
     assert status in (1, 2, 3, 4), status
+    assert host_word in (1, 2, 3, 4), host_word
     out, kernel = _run(_native.POLICY_TENSOR_CORE, guide, value, weight, bias, 17)
     exp = c_oracle.forward(guide, value, weight, bias, offsets)
     assert normwise_err(out, exp) <= TC_TOL[torch.bfloat16]
+    assert _native.device_status(clear=True) == 0
+
+
+def test_expired_wait_reaches_python_through_the_module(cuda_lib):
+    """The product path surfaces an expired wait by itself: the launch that
+    gave up writes the host-visible status word, and the module's next call
+    raises ExpiredWaitError (no device_status() call by the user); the call
+    after that runs normally and is correct."""
+    lib = _native.load()
+    guide, value, weight, bias = _inputs(1, 8, 16, 64, 17, torch.bfloat16, seed=22)
+    torch.manual_seed(0)
+    la = LocalAttender(64, 17).to(DEV).to(torch.bfloat16)
+    with torch.no_grad():
+        la.conv1.weight.copy_(weight.reshape(17, 64, 1, 1))
+        la.conv1.bias.copy_(bias)
+    g, v = guide.to(DEV), value.to(DEV)
+    with torch.no_grad():
+        la(g, v)  # registers the host status word
+        torch.cuda.synchronize()
+        _native.check(lib.uplift_la_test_hook(1, 20_000_000), "test hook")
+        try:
+            la(g, v)
+            torch.cuda.synchronize()
+        finally:
+            lib.uplift_la_test_hook(0, 0)
+        with pytest.raises(_native.ExpiredWaitError):
+            la(g, v)
+        out = la(g, v)
+        torch.cuda.synchronize()
+    offsets, _ = neighbourhood(17)
+    exp = c_oracle.forward(guide, value, la.conv1.weight.detach().float().reshape(17, 64).cpu(),
+                           la.conv1.bias.detach().float().cpu(), offsets)
+    assert normwise_err(out, exp) <= TC_TOL[torch.bfloat16]
+    assert _native.host_status.value() == 0
     assert _native.device_status(clear=True) == 0

@@ -116,10 +116,13 @@ def test_tcw_expired_wait_is_reported_and_context_survives(cuda_lib):
     try:
         _, kernel = _run(_native.POLICY_TENSOR_CORE, guide, value, weight, bias, 17)  # synchronises
         status = _native.device_status(clear=True)
+        host_word = _native.host_status.value()
+        _native.host_status.clear()  # this test reads the device copy itself
     finally:
         lib.uplift_la_test_hook(0, 0)
     assert kernel == _native.KERNEL_TENSOR_CORE_WIDE
     assert status in (1, 2, 3, 4), status
+    assert host_word in (1, 2, 3, 4), host_word
     out, _ = _run(_native.POLICY_TENSOR_CORE, guide, value, weight, bias, 17)
     exp = c_oracle.forward(guide, value, weight, bias, offsets)
     assert normwise_err(out, exp) <= TIGHT

@@ -30,6 +30,7 @@ EXPORTED = (
     "uplift_la_last_kernel",
     "uplift_la_device_status",
     "uplift_la_test_hook",
+    "uplift_la_set_host_status_word",
     "uplift_la_backward",
     "uplift_la_backward_noalloc",
     # include/uplift_glue.h
@@ -94,6 +95,8 @@ def load(build_if_missing: bool = False):
         lib.uplift_la_device_status.argtypes = [i]
         lib.uplift_la_test_hook.restype = i
         lib.uplift_la_test_hook.argtypes = [i, ctypes.c_ulonglong]
+        lib.uplift_la_set_host_status_word.restype = i
+        lib.uplift_la_set_host_status_word.argtypes = [vp]
         lib.uplift_la_backward.restype = i
         lib.uplift_la_backward.argtypes = [vp, i64p, vp, i64p, vp, i64p, fp, fp, fp, vp, i64p, vp, i64p,
                                            fp, fp, i, i, i, i, i, i, i, i8p, i, i, i, i, vp]
@@ -158,3 +161,60 @@ def last_kernel() -> int:
 def device_status(clear: bool = True) -> int:
     """0 if every tensor-core launch completed its pipeline (synchronises)."""
     return load().uplift_la_device_status(int(clear))
+
+
+ROLES = {1: "producer", 2: "MMA issuer", 3: "softmax / split", 4: "epilogue"}
+
+
+class ExpiredWaitError(RuntimeError):
+    """A tensor-core launch gave up on a bounded wait: the tiles it had not
+    finished were never written, so that launch's output is incomplete."""
+
+
+class HostStatus:
+    """The host-visible status word of the tensor-core kernels
+    (uplift_la_set_host_status_word): one pinned int32 that a launch whose
+    bounded wait expired writes the failing role into.  Registered on the
+    first kernel launch of the process; `raise_if_set()` is a plain memory
+    read (no synchronisation), called before every launch, so an expiry
+    surfaces as ExpiredWaitError at the first call after the failed kernel
+    has finished."""
+
+    def __init__(self):
+        self._buf = None
+        self._word = None
+
+    def ensure(self):
+        if self._buf is None:
+            import torch
+            with _lock:
+                if self._buf is None:
+                    buf = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+                    check(load().uplift_la_set_host_status_word(buf.data_ptr()),
+                          "uplift_la_set_host_status_word")
+                    self._word = ctypes.c_uint32.from_address(buf.data_ptr())
+                    self._buf = buf
+
+    def value(self) -> int:
+        return 0 if self._word is None else int(self._word.value)
+
+    def clear(self) -> None:
+        if self._word is not None:
+            self._word.value = 0
+
+    def raise_if_set(self) -> None:
+        if self._word is None:
+            import torch
+            if not torch.cuda.is_current_stream_capturing():  # no host allocation inside a capture
+                self.ensure()
+            return
+        code = self._word.value
+        if code:
+            self._word.value = 0
+            load().uplift_la_device_status(1)  # clear the device copy too (error path: synchronises)
+            raise ExpiredWaitError(
+                f"a Local Attender tensor-core launch on this process gave up after a bounded wait "
+                f"(role: {ROLES.get(code, code)}); its output is incomplete and must not be used")
+
+
+host_status = HostStatus()

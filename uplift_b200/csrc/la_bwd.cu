@@ -11,6 +11,44 @@
 
 #include "la_bwd.cuh"
 
+namespace {
+
+// Argument checks shared by both backward entry points (everything except
+// the workspace pointer, which only uplift_la_backward takes).
+int check_backward_args(const void* dout, const int64_t dout_strides[4], const void* guide,
+                        const int64_t guide_strides[4], const void* value, const int64_t value_strides[4],
+                        const float* weight, const void* dguide, const int64_t dguide_strides[4],
+                        const void* dvalue, const int64_t dvalue_strides[4], int B, int Cg, int C, int H, int W,
+                        int I, int K, const int8_t* offsets, int pn, int dtype) {
+  using ula::fail;
+  if (dtype != UPLIFT_LA_F32 && dtype != UPLIFT_LA_BF16 && dtype != UPLIFT_LA_F16)
+    return fail(UPLIFT_LA_ERR_ARG, "unknown dtype %d", dtype);
+  if (B < 0 || Cg < 1 || C < 1 || H < 0 || W < 0 || I < 1)
+    return fail(UPLIFT_LA_ERR_SHAPE, "bad sizes B=%d Cg=%d C=%d H=%d W=%d I=%d", B, Cg, C, H, W, I);
+  if (K < 1 || K > UPLIFT_LA_MAX_K) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d out of range", K);
+  if (pn < 0 || pn > UPLIFT_LA_MAX_PN) return fail(UPLIFT_LA_ERR_OFFSETS, "pn=%d out of range", pn);
+  if (offsets == nullptr || dout_strides == nullptr || guide_strides == nullptr || value_strides == nullptr)
+    return fail(UPLIFT_LA_ERR_ARG, "null offsets or strides");
+  if ((dguide != nullptr && dguide_strides == nullptr) || (dvalue != nullptr && dvalue_strides == nullptr))
+    return fail(UPLIFT_LA_ERR_ARG, "null gradient strides");
+  const int64_t npix = (int64_t)B * I * H * I * W;
+  if (npix > 0 && (dout == nullptr || guide == nullptr || value == nullptr || weight == nullptr))
+    return fail(UPLIFT_LA_ERR_ARG, "null input pointer");
+  if (npix >= ((int64_t)1 << 40)) return fail(UPLIFT_LA_ERR_SHAPE, "too many pixels");
+  for (int k = 0; k < K; ++k) {
+    const int dy = offsets[2 * k], dx = offsets[2 * k + 1];
+    if (dy < -pn || dy > pn || dx < -pn || dx > pn)
+      return fail(UPLIFT_LA_ERR_OFFSETS, "offset %d = (%d, %d) exceeds pn=%d", k, dy, dx, pn);
+  }
+  const int64_t* st[5] = {dout_strides, guide_strides, value_strides, dguide_strides, dvalue_strides};
+  for (int i = 0; i < 5; ++i)
+    if (st[i] != nullptr && st[i][1] != 1 && !(i == 1 || i == 3 ? Cg == 1 : C == 1))
+      return fail(UPLIFT_LA_ERR_LAYOUT, "tensors need channel stride 1 (channels_last)");
+  return UPLIFT_LA_OK;
+}
+
+}  // namespace
+
 extern "C" int uplift_la_backward(const void* dout, const int64_t dout_strides[4],
                                   const void* guide, const int64_t guide_strides[4],
                                   const void* value, const int64_t value_strides[4],
@@ -24,33 +62,17 @@ extern "C" int uplift_la_backward(const void* dout, const int64_t dout_strides[4
                                   void* stream) {
   using namespace ula;
   using ula::bwd::Args;
-  if (dtype != UPLIFT_LA_F32 && dtype != UPLIFT_LA_BF16 && dtype != UPLIFT_LA_F16)
-    return fail(UPLIFT_LA_ERR_ARG, "unknown dtype %d", dtype);
-  if (B < 0 || Cg < 1 || C < 1 || H < 0 || W < 0 || I < 1)
-    return fail(UPLIFT_LA_ERR_SHAPE, "bad sizes B=%d Cg=%d C=%d H=%d W=%d I=%d", B, Cg, C, H, W, I);
-  if (K < 1 || K > UPLIFT_LA_MAX_K) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d out of range", K);
-  if (pn < 0 || pn > UPLIFT_LA_MAX_PN) return fail(UPLIFT_LA_ERR_OFFSETS, "pn=%d out of range", pn);
-  if (offsets == nullptr || dout_strides == nullptr || guide_strides == nullptr || value_strides == nullptr)
-    return fail(UPLIFT_LA_ERR_ARG, "null offsets or strides");
-  if ((dguide != nullptr && dguide_strides == nullptr) || (dvalue != nullptr && dvalue_strides == nullptr))
-    return fail(UPLIFT_LA_ERR_ARG, "null gradient strides");
+  const int rc = check_backward_args(dout, dout_strides, guide, guide_strides, value, value_strides, weight, dguide,
+                                     dguide_strides, dvalue, dvalue_strides, B, Cg, C, H, W, I, K, offsets, pn, dtype);
+  if (rc != UPLIFT_LA_OK) return rc;
   const int64_t npix = (int64_t)B * I * H * I * W;
-  if (npix > 0 && (dout == nullptr || guide == nullptr || value == nullptr || weight == nullptr || probs == nullptr))
-    return fail(UPLIFT_LA_ERR_ARG, "null input pointer");
-  if (npix >= ((int64_t)1 << 40)) return fail(UPLIFT_LA_ERR_SHAPE, "too many pixels");
+  if (npix > 0 && probs == nullptr) return fail(UPLIFT_LA_ERR_ARG, "null workspace pointer");
   Args a;
   memset(&a, 0, sizeof(a));
   for (int k = 0; k < K; ++k) {
-    const int dy = offsets[2 * k], dx = offsets[2 * k + 1];
-    if (dy < -pn || dy > pn || dx < -pn || dx > pn)
-      return fail(UPLIFT_LA_ERR_OFFSETS, "offset %d = (%d, %d) exceeds pn=%d", k, dy, dx, pn);
-    a.dy[k] = (int8_t)dy;
-    a.dx[k] = (int8_t)dx;
+    a.dy[k] = offsets[2 * k];
+    a.dx[k] = offsets[2 * k + 1];
   }
-  const int64_t* st[5] = {dout_strides, guide_strides, value_strides, dguide_strides, dvalue_strides};
-  for (int i = 0; i < 5; ++i)
-    if (st[i] != nullptr && st[i][1] != 1 && !(i == 1 || i == 3 ? Cg == 1 : C == 1))
-      return fail(UPLIFT_LA_ERR_LAYOUT, "tensors need channel stride 1 (channels_last)");
   a.dout = dout; a.d_b = dout_strides[0]; a.d_h = dout_strides[2]; a.d_w = dout_strides[3];
   a.guide = guide; a.g_b = guide_strides[0]; a.g_h = guide_strides[2]; a.g_w = guide_strides[3];
   a.value = value; a.v_b = value_strides[0]; a.v_h = value_strides[2]; a.v_w = value_strides[3];
@@ -178,9 +200,10 @@ extern "C" int uplift_la_backward_noalloc(const void* dout, const int64_t dout_s
                                           const int8_t* offsets, int pn, int conv_res, int dtype, int hardmax,
                                           void* stream) {
   using namespace ula;
-  if (B < 0 || H < 0 || W < 0 || I < 1 || K < 1 || K > UPLIFT_LA_MAX_K)
-    return fail(UPLIFT_LA_ERR_SHAPE, "uplift_la_backward_noalloc: bad sizes B=%d H=%d W=%d I=%d K=%d", B, H, W, I,
-                K);
+  // the arguments first, so that an invalid call names its bad argument
+  const int rc = check_backward_args(dout, dout_strides, guide, guide_strides, value, value_strides, weight, dguide,
+                                     dguide_strides, dvalue, dvalue_strides, B, Cg, C, H, W, I, K, offsets, pn, dtype);
+  if (rc != UPLIFT_LA_OK) return rc;
   // B * (I*H) * (I*W) * K floats, checked factor by factor against the maximum
   const long long cap = UPLIFT_LA_NOALLOC_MAX_PROBS;
   long long need = 1;

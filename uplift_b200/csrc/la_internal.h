@@ -43,6 +43,11 @@ bool tcw_eligible(const TcArgs& a, const char** why);
 int tcw_launch(const TcArgs& a, cudaStream_t stream);
 int tcw_device_status(bool clear);
 
+// Host-visible status word registered by the caller
+// (uplift_la_set_host_status_word), or null; passed to every tensor-core
+// launch so that an expired wait is also written there.
+unsigned int* host_status_word();
+
 // Record an error message for uplift_la_last_error().
 int fail(int code, const char* fmt, ...);
 

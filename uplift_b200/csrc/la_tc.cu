@@ -41,6 +41,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "uplift_la.h"
 #include "la_internal.h"
@@ -54,9 +55,10 @@ __device__ unsigned int g_tc_status;
 
 namespace tc {
 
-// Test hook state (uplift_la_test_hook): a fault mode and a wait limit.
-int g_test_fault = 0;
-uint64_t g_test_timeout_ns = 0;
+// Test hook state (uplift_la_test_hook): a fault mode and a wait limit
+// (process-wide; atomics, since any host thread may launch).
+std::atomic<int> g_test_fault{0};
+std::atomic<unsigned long long> g_test_timeout_ns{0};
 
 constexpr int kCellsY = 4, kCellsX = 8;      // cells per tile
 constexpr int kM = 128;                      // output pixels per tile (8 x 16)
@@ -106,13 +108,14 @@ struct Params {
   int hardmax;
   int margin;           // max |offset| (cells this close to a border may clamp)
   uint64_t timeout_ns;  // limit of every mbarrier wait
+  unsigned int* host_status;  // host-visible status word or null
   int test_fault;       // 1: the guide producer issues no loads (tests the timeout path)
 };
 
 // Bounded mbarrier wait recording expiries in this kernel's status word.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, unsigned where,
-                                          uint64_t limit_ns) {
-  return mbar_wait_status(b, parity, abort_flag, where, limit_ns, &g_tc_status);
+                                          const WaitLimit& limit) {
+  return mbar_wait_status(b, parity, abort_flag, where, limit, &g_tc_status);
 }
 
 template <typename T> struct Store;
@@ -227,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
 
   int local_tiles = 0;
   for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) ++local_tiles;
-  const uint64_t tmo = p.timeout_ns;
+  const WaitLimit tmo{p.timeout_ns, p.host_status};
   const int half_chunks = (p.nchunks + 1) / 2;
 
   if (warp == 0 || warp == kGuideWarp) {
@@ -543,12 +546,13 @@ namespace tc {
 template <typename T, int K>
 int launch_t(const Params& p, int dev, int grid, cudaStream_t stream) {
   auto fn = la_tc_kernel<T, K>;
-  // the shared-memory opt-in is per function and device; set it once
-  static bool configured[64] = {};
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
+  // the shared-memory opt-in is per function and device; set it once (two
+  // threads racing here both set the same value, which is harmless)
+  static std::atomic<bool> configured[64] = {};
+  if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    if (dev >= 0 && dev < 64) configured[dev] = true;
+    if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -582,13 +586,13 @@ int launch_k(const Params& p, int K, int dev, int grid, cudaStream_t stream) {
 
 int tc_set_test_hook(int fault, unsigned long long timeout_ns) {
   if (fault < 0 || fault > 1) return fail(UPLIFT_LA_ERR_ARG, "unknown test fault %d", fault);
-  tc::g_test_fault = fault;
-  tc::g_test_timeout_ns = timeout_ns;
+  tc::g_test_timeout_ns.store(timeout_ns);
+  tc::g_test_fault.store(fault);
   return UPLIFT_LA_OK;
 }
 
-int tc_test_fault() { return tc::g_test_fault; }
-unsigned long long tc_test_timeout_ns() { return tc::g_test_timeout_ns; }
+int tc_test_fault() { return tc::g_test_fault.load(); }
+unsigned long long tc_test_timeout_ns() { return tc::g_test_timeout_ns.load(); }
 
 int tc_device_status(bool clear) {
   unsigned int v = 0;
@@ -652,17 +656,18 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
   if (nt >= (1ll << 31)) return fail(UPLIFT_LA_ERR_SHAPE, "too many tiles");
   p.num_tiles = (int)nt;
   p.res_k = a.conv_res ? std::min(a.K, a.Cg) : 0;
-  p.timeout_ns = g_test_timeout_ns != 0 ? g_test_timeout_ns : kTimeoutNs;
-  p.test_fault = g_test_fault;
+  p.timeout_ns = tc_test_timeout_ns() != 0 ? tc_test_timeout_ns() : kTimeoutNs;
+  p.host_status = host_status_word();
+  p.test_fault = tc_test_fault();
   p.hardmax = a.hardmax;
   p.margin = margin;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(UPLIFT_LA_ERR_NO_DEVICE, "cudaGetDevice failed");
-  static int sm_count[64] = {};
-  int sms = (dev >= 0 && dev < 64) ? sm_count[dev] : 0;
+  static std::atomic<int> sm_count[64] = {};
+  int sms = (dev >= 0 && dev < 64) ? sm_count[dev].load(std::memory_order_relaxed) : 0;
   if (sms == 0) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (dev >= 0 && dev < 64) sm_count[dev] = sms;
+    if (dev >= 0 && dev < 64) sm_count[dev].store(sms, std::memory_order_relaxed);
   }
   const int grid = (int)std::min<int64_t>(nt, std::max(sms, 1));
   return a.dtype == UPLIFT_LA_BF16 ? launch_k<__nv_bfloat16>(p, a.K, dev, grid, stream)

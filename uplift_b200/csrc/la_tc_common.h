@@ -39,20 +39,33 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Limit of every bounded wait of a launch, and the optional host-visible
+// status word (pinned host memory registered by the caller) that an expiry
+// is also written to, so that the host learns of it without synchronising.
+struct WaitLimit {
+  uint64_t ns;
+  unsigned int* host_word;  // null: none registered
+};
+
 // Bounded wait for the phase of parity `parity` to complete.  Returns false
-// (after flagging the CTA and recording `where` in the status word) on
-// timeout, or when another role of the CTA has already given up.
+// (after flagging the CTA and recording `where` in the status word and the
+// host word) on timeout, or when another role of the CTA has already given
+// up.
 static __device__ __noinline__ bool mbar_wait_status(uint64_t* b, uint32_t parity, volatile int* abort_flag, unsigned where,
-                                             uint64_t limit_ns, unsigned int* status) {
+                                                     WaitLimit limit, unsigned int* status) {
   if (mbar_try(b, parity)) return true;
   const uint64_t t0 = gtimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try(b, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort_flag) return false;
-      if (gtimer() - t0 > limit_ns) {
+      if (gtimer() - t0 > limit.ns) {
         *abort_flag = 1;
         atomicCAS(status, 0u, where);
+        if (limit.host_word != nullptr) {
+          *reinterpret_cast<volatile unsigned int*>(limit.host_word) = where;
+          __threadfence_system();
+        }
         return false;
       }
     }

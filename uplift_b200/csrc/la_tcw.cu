@@ -50,6 +50,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "uplift_la.h"
 #include "la_internal.h"
@@ -106,12 +107,13 @@ struct Params {
   int Cg, C, H, W, nchunks, tiles_x, tiles_y, num_tiles;
   int conv_res, hardmax;
   uint64_t timeout_ns;
+  unsigned int* host_status;  // host-visible status word or null
   int test_fault;  // 1: the producer issues no loads (tests the timeout path)
 };
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, unsigned where,
-                                          uint64_t limit_ns) {
-  return mbar_wait_status(b, parity, abort_flag, where, limit_ns, &g_tcw_status);
+                                          const WaitLimit& limit) {
+  return mbar_wait_status(b, parity, abort_flag, where, limit, &g_tcw_status);
 }
 
 // kind::f16 MMA with the A operand read from TMEM (lane = row; a 32-bit
@@ -243,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tcw_kernel(const __grid_consta
 
   int local_tiles = 0;
   for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) ++local_tiles;
-  const uint64_t tmo = p.timeout_ns;
+  const WaitLimit tmo{p.timeout_ns, p.host_status};
   const int nch = p.nchunks;
 
   if (warp == 0) {
@@ -436,12 +438,12 @@ template <int K>
 int launch_t(const Params& p, int dev, int grid, cudaStream_t stream) {
   auto fn = la_tcw_kernel<K>;
   const int smem = smem_bytes(K, p.nchunks);
-  static bool configured[64] = {};
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
+  static std::atomic<bool> configured[64] = {};  // racing threads set the same value
+  if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          smem_bytes(K, kMaxCg / kChunkCh));
     if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    if (dev >= 0 && dev < 64) configured[dev] = true;
+    if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -508,14 +510,15 @@ int tcw_launch(const TcArgs& a, cudaStream_t stream) {
   p.conv_res = a.conv_res;
   p.hardmax = a.hardmax;
   p.timeout_ns = tc_test_timeout_ns() != 0 ? tc_test_timeout_ns() : kTimeoutNs;
+  p.host_status = host_status_word();
   p.test_fault = tc_test_fault();
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(UPLIFT_LA_ERR_NO_DEVICE, "cudaGetDevice failed");
-  static int sm_count[64] = {};
-  int sms = (dev >= 0 && dev < 64) ? sm_count[dev] : 0;
+  static std::atomic<int> sm_count[64] = {};
+  int sms = (dev >= 0 && dev < 64) ? sm_count[dev].load(std::memory_order_relaxed) : 0;
   if (sms == 0) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (dev >= 0 && dev < 64) sm_count[dev] = sms;
+    if (dev >= 0 && dev < 64) sm_count[dev].store(sms, std::memory_order_relaxed);
   }
   const int grid = (int)std::min<int64_t>(nt, std::max(sms, 1));
   switch (a.K) {

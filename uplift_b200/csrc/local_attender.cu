@@ -10,6 +10,8 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 #include <type_traits>
 
 #include "uplift_la.h"
@@ -22,6 +24,11 @@ namespace ula {
 thread_local char g_err[512] = "";
 thread_local int g_last_kernel = 0;
 int g_policy = UPLIFT_LA_POLICY_AUTO;
+// Host-visible status word registered by uplift_la_set_host_status_word
+// (pinned host memory; null = none).
+std::atomic<unsigned int*> g_host_status{nullptr};
+
+unsigned int* host_status_word() { return g_host_status.load(std::memory_order_acquire); }
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -76,7 +83,11 @@ int device_info(DevInfo* info) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_NO_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
   static DevInfo cache[64];
-  if (dev < 64 && cache[dev].sms > 0) { *info = cache[dev]; return UPLIFT_LA_OK; }
+  static std::mutex mu;  // launches may come from any host thread
+  if (dev >= 0 && dev < 64) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (cache[dev].sms > 0) { *info = cache[dev]; return UPLIFT_LA_OK; }
+  }
   int sms = 0, major = 0, optin = 0;
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
@@ -85,7 +96,10 @@ int device_info(DevInfo* info) {
   if (major != 10) return fail(UPLIFT_LA_ERR_NO_DEVICE, "device %d has compute capability %d.x; this build targets sm_100a", dev, major);
   info->sms = sms;
   info->max_smem_optin = (size_t)optin;
-  if (dev < 64) cache[dev] = *info;
+  if (dev >= 0 && dev < 64) {
+    std::lock_guard<std::mutex> lock(mu);
+    cache[dev] = *info;
+  }
   return UPLIFT_LA_OK;
 }
 
@@ -309,6 +323,11 @@ int uplift_la_device_status(int clear) {
   return a != 0 ? a : b;
 }
 
+int uplift_la_set_host_status_word(unsigned int* word) {
+  ula::g_host_status.store(word, std::memory_order_release);
+  return UPLIFT_LA_OK;
+}
+
 int uplift_la_test_hook(int fault, unsigned long long wait_limit_ns) {
   return ula::tc_set_test_hook(fault, wait_limit_ns);
 }
@@ -328,6 +347,6 @@ const char* uplift_la_status_string(int status) {
   }
 }
 
-int uplift_la_abi_version(void) { return (1 << 16) | 1; }
+int uplift_la_abi_version(void) { return (1 << 16) | 2; }
 
 }  // extern "C"

@@ -91,6 +91,7 @@ def local_attender_raw(guide: torch.Tensor, value: torch.Tensor, weight: torch.T
         out = torch.empty((B, C, Ho, Wo), dtype=value.dtype, device=dev,
                           memory_format=torch.channels_last)
     lib = _native.load()
+    _native.host_status.raise_if_set()
     stream = torch.cuda.current_stream(dev).cuda_stream
     with torch.cuda.device(dev):
         rc = lib.uplift_la_forward(
