@@ -1,9 +1,9 @@
 """Generate the Local Attender golden vectors by EXECUTING THE REFERENCE.
 
-Run in a container that has the reference checkout (read-only) at
-/root/reference:
+Run where a checkout of the reference is available, naming it with --ref
+or the UPLIFT_REFERENCE environment variable:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <reference checkout>
 
 It loads uplift/uplift.py (LocalAttender, uplift/uplift.py:740-847) and
 uplift/kernels/triton_attender.py (TritonLocalAttender._fallback_forward,
@@ -27,6 +27,7 @@ from __future__ import annotations
 
 import argparse
 import hashlib
+import os
 import importlib.util
 import sys
 from pathlib import Path
@@ -161,8 +162,11 @@ def model_golden(ref: Path, up):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("UPLIFT_REFERENCE"),
+                    help="reference checkout (default: $UPLIFT_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("name the reference checkout with --ref or UPLIFT_REFERENCE")
     ref = Path(args.ref)
     up = load_module("ref_uplift_model", ref / "uplift" / "uplift.py")
     tri = load_module("ref_triton_attender", ref / "uplift" / "kernels" / "triton_attender.py")

@@ -41,13 +41,13 @@ def test_make_fast_compiled_matches_plain(cuda_lib):
     img = torch.rand(2, 3, 112, 112, generator=g).to(DEV, torch.bfloat16)
     feats = torch.randn(2, 384, 8, 8, generator=g).to(DEV, torch.bfloat16)
     old = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
-    try:  # make_fast(compile=True) switches TF32 on globally
-        fast = make_fast(m, compile=True, compile_mode="default", warmup=False, device=torch.device(DEV))
-        with torch.no_grad():
-            ref = m(img, feats)
-        out = fast(img, feats)
-        torch.cuda.synchronize()
-    finally:
-        torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = old
+    # allow_tf32=True: TF32 inside the fast forward only, the globals untouched
+    fast = make_fast(m, compile=True, compile_mode="default", warmup=False, device=torch.device(DEV),
+                     allow_tf32=True)
+    with torch.no_grad():
+        ref = m(img, feats)
+    out = fast(img, feats)
+    torch.cuda.synchronize()
+    assert (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32) == old
     err = ((out.float() - ref.float()).abs().max() / ref.float().abs().max()).item()
     assert out.shape == ref.shape and err <= 2e-2, err  # bf16 convs, folded BatchNorm

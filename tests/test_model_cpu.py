@@ -52,3 +52,30 @@ def test_hub_signatures():
     assert isinstance(m, UPLiFT) and m.attender.num_connected == 17
     with pytest.raises(ValueError, match="Unknown variant"):
         hubconf.uplift("nope", pretrained=False, include_extractor=False)
+
+
+def test_tf32_mode_scopes_the_switches():
+    """allow_tf32 on the model and on make_fast sets TF32 for the forward
+    only and leaves PyTorch's global switches as they were; None (the
+    reference's behaviour) touches nothing."""
+    from uplift_b200.fast import make_fast
+    from uplift_b200.uplift import tf32_mode
+    old = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+    try:
+        torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = True, True
+        with tf32_mode(False):
+            assert (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32) == (False, False)
+        assert (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32) == (True, True)
+        with tf32_mode(None):
+            assert (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32) == (True, True)
+        cfg = get_config("dinov2-s14")
+        torch.manual_seed(0)
+        model = UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift, allow_tf32=False)
+        torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = False, True
+        fast = make_fast(model, compile=False, warmup=False, device=torch.device("cpu"))
+        assert fast.allow_tf32 is False  # inherited from the model
+        fast = make_fast(model, compile=False, warmup=False, device=torch.device("cpu"), allow_tf32=True)
+        assert fast.allow_tf32 is True
+        assert (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32) == (False, True)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = old

@@ -19,19 +19,12 @@ def model_golden():
     return torch.load(GOLDEN / "model_cases.pt", weights_only=False)
 
 
-@pytest.fixture(autouse=True)
-def no_tf32():
-    old = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
-    torch.backends.cuda.matmul.allow_tf32 = False
-    torch.backends.cudnn.allow_tf32 = False
-    yield
-    torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = old
-
-
 def _model(variant, iters):
+    """fp32 model in the fp32-exact mode (TF32 off inside every forward;
+    make_fast inherits the setting)."""
     cfg = get_config(variant)
     torch.manual_seed(0)
-    m = U.UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift).eval()
+    m = U.UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift, allow_tf32=False).eval()
     m.enable_iterative(iters)
     return m.to(DEV)
 

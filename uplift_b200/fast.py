@@ -33,16 +33,28 @@ from .attender import AttenderWrapper, LocalAttender
 
 def make_fast(model: nn.Module, image_size: Optional[int] = None, compile: bool = True,
               compile_mode: str = "max-autotune", warmup: bool = True,
-              device: Optional[torch.device] = None) -> nn.Module:
-    """Optimise a UPLiFT model for inference (see module docstring)."""
+              device: Optional[torch.device] = None, allow_tf32: Optional[bool] = None) -> nn.Module:
+    """Optimise a UPLiFT model for inference (see module docstring).
+
+    `allow_tf32` (an addition to the reference's signature): None takes the
+    model's own setting (UPLiFT(..., allow_tf32=...)) and, when that is
+    None too, does what the reference does -- compile=True switches TF32 on
+    globally (uplift/fast.py:122-124).  False gives an fp32-exact fast mode:
+    every forward runs with TF32 off (BatchNorm folded, channels_last, fused
+    kernels) and the global switches are left as they were; True runs every
+    forward with TF32 on, also without touching the globals."""
     if device is None:
         device = torch.device("cuda" if torch.cuda.is_available() else "cpu")
+    if allow_tf32 is None:
+        allow_tf32 = getattr(model, "allow_tf32", None)
     fast = OptimizedUPLiFT(model, device=device)
+    fast.allow_tf32 = allow_tf32
     if isinstance(fast.model.attender, LocalAttender):
         fast.model.attender = AttenderWrapper(fast.model.attender).to(device).eval()
     if compile:
-        torch.backends.cuda.matmul.allow_tf32 = True
-        torch.backends.cudnn.allow_tf32 = True
+        if allow_tf32 is None:
+            torch.backends.cuda.matmul.allow_tf32 = True
+            torch.backends.cudnn.allow_tf32 = True
         fast._compiled_forward = torch.compile(fast._forward_impl, mode=compile_mode)
     if warmup and image_size is not None and compile:
         _warmup(fast, image_size, device)
@@ -60,12 +72,14 @@ class OptimizedUPLiFT(nn.Module):
         self.model = self.model.to(device=device)
         self.model = self.model.to(memory_format=torch.channels_last)
         self._compiled_forward = None
+        self.allow_tf32 = None  # set by make_fast
 
     @torch.inference_mode()
     def forward(self, img, x, outsize=None):
-        if self._compiled_forward is not None:
-            return self._compiled_forward(img, x, outsize)
-        return self._forward_impl(img, x, outsize)
+        with U.tf32_mode(self.allow_tf32):
+            if self._compiled_forward is not None:
+                return self._compiled_forward(img, x, outsize)
+            return self._forward_impl(img, x, outsize)
 
     def _forward_impl(self, img, x, outsize=None):
         """The iteration loop of UPLiFT.forward (as the reference's fast path,

@@ -11,7 +11,7 @@ outsize), compiled.
 """
 from __future__ import annotations
 
-from typing import Callable
+from typing import Callable, Optional
 
 import torch
 import torch.nn as nn
@@ -335,13 +335,47 @@ class UPLiFTDecoder(nn.Module):
         return residual_auto(x, y) if self.residual_outc else y
 
 
+class tf32_mode:
+    """Scope the TF32 switches of cuDNN convolutions and matmuls to a block:
+    allow=True / False sets both for the block and restores the previous
+    values after it; allow=None leaves them as they are.  The switches are
+    process-wide, so blocks that run at the same time in several host
+    threads see each other's settings."""
+
+    def __init__(self, allow: Optional[bool]):
+        self.allow = allow
+        self._old = None
+
+    def __enter__(self):
+        if self.allow is not None:
+            self._old = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+            torch.backends.cuda.matmul.allow_tf32 = bool(self.allow)
+            torch.backends.cudnn.allow_tf32 = bool(self.allow)
+        return self
+
+    def __exit__(self, *exc):
+        if self._old is not None:
+            torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = self._old
+            self._old = None
+        return False
+
+
 class UPLiFT(nn.Module):
     """Iterative feature upsampler (uplift/uplift.py:537-709).  Each
     iteration: encoder (once with enc_share) -> decoder -> guide -> fused
-    Local Attender (value = previous features) -> optional refiner."""
+    Local Attender (value = previous features) -> optional refiner.
 
-    def __init__(self, in_channels, patch_size, cfg, dtype: torch.dtype = torch.float32, low_mem=False):
+    `allow_tf32` (not in the reference, which leaves PyTorch's global
+    switches alone): None keeps the global settings (PyTorch's default lets
+    cuDNN convolutions round fp32 operands to TF32); False runs every
+    forward with TF32 off -- the fp32-exact mode the fp32 parity
+    requirement (1e-4) needs -- and True with TF32 on; either way the global
+    switches are restored after the call."""
+
+    def __init__(self, in_channels, patch_size, cfg, dtype: torch.dtype = torch.float32, low_mem=False,
+                 allow_tf32: Optional[bool] = None):
         super().__init__()
+        self.allow_tf32 = allow_tf32
         self.in_channels = in_channels
         self.patch_size = patch_size
         self.cfg = cfg
@@ -395,6 +429,10 @@ class UPLiFT(nn.Module):
         return x, enc_feats
 
     def forward(self, img, x, outsize=None):
+        with tf32_mode(self.allow_tf32):
+            return self._forward(img, x, outsize)
+
+    def _forward(self, img, x, outsize=None):
         steps = []
         ex_feats = None
         for i in range(self.iters):
