@@ -75,6 +75,33 @@ def load_traffic():
     return None
 
 
+REF_ROOT = ROOT / "baseline" / "_ref"
+
+
+def reference_modules(*names):
+    """Submodules of the unmodified reference package, pip-installed under
+    baseline/_ref, e.g. reference_modules("uplift", "fast") -> ([uplift.uplift,
+    uplift.fast], None); ([], reason) when it is absent or fails to import.
+    The package's __init__ imports the feature extractor, which needs
+    omegaconf (not installed, and not on the attender's path), so a bare
+    package object whose __path__ is the installed directory is registered
+    first and the submodules are imported from it as they are."""
+    import importlib
+    import types
+    pkg_dir = REF_ROOT / "uplift"
+    if not (pkg_dir / "uplift.py").exists():
+        return [], f"reference not installed under {REF_ROOT.relative_to(ROOT)}"
+    cur = sys.modules.get("uplift")
+    if cur is None or list(getattr(cur, "__path__", [])) != [str(pkg_dir)]:
+        pkg = types.ModuleType("uplift")
+        pkg.__path__ = [str(pkg_dir)]
+        sys.modules["uplift"] = pkg
+    try:
+        return [importlib.import_module("uplift." + n) for n in names], None
+    except Exception as e:  # noqa: BLE001 -- reported, not raised: the bench line still prints
+        return [], f"reference import failed: {type(e).__name__}: {e}"[:200]
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled during the timed region."""
 
@@ -153,6 +180,17 @@ def max_over_ranks(x: float, world: int, dev) -> float:
     t = torch.tensor([x], dtype=torch.float64, device=dev)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     return float(t.item())
+
+
+def workload_config(world):
+    """The `config` object of both arms' JSON lines."""
+    return {"workload": "dinov2-s14-448-iters4 Local Attender chain",
+            "images_per_gpu": B_PER_GPU, "global_images": B_PER_GPU * world,
+            "K": K_NBR, "guide_channels": CG, "value_channels": C, "scale": 2,
+            "levels": [f"{c}^2->{f}^2" for c, f in LEVELS],
+            "out_mpix_per_step_per_gpu": round(out_pixels() / 1e6, 4),
+            "l2": "inputs larger than L2 (3.03 GB algorithmic per step), no flush",
+            "parallelism": f"batch-sharded x{world}, no data-path collective"}
 
 
 def make_inputs(dev, B=None, seed=0):
@@ -261,11 +299,17 @@ def run_ours(args, world, rank, local):
     peak, peak_kind = load_peaks()
     traffic = load_traffic()
 
+    # ---- the reference's own GPU path (Triton) on the same chain
+    triton = None
+    if not args.no_triton:
+        triton = run_triton_reference(dev, stream, la, value0, guides, outs[-1], ms_step)
+
     # ---- end to end through the public module with pinned host buffers
     e2e = None if args.no_e2e else run_e2e(la, host, dev, stream, world, args, mpix_step)
 
     # ---- whole upsampler throughput (weak scaling: 8 images per GPU)
-    ups = None if args.no_upsampler else run_upsampler(dev, stream, world, rank, args, outsize=1022)
+    ups = None if args.no_upsampler else run_upsampler(dev, stream, world, rank, args, outsize=1022,
+                                                       gather=not args.no_gather)
     models = None if args.no_upsampler else run_model_configs(dev, stream, world, rank, args)
 
     # ---- fp32 attender configurations (standalone K=9 call, SD1.5-VAE levels)
@@ -284,13 +328,7 @@ def run_ours(args, world, rank, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seed 0, N(0,1) guides/values, random-init LocalAttender(64,17) in bf16)",
-        "config": {"workload": "dinov2-s14-448-iters4 Local Attender chain",
-                   "images_per_gpu": B_PER_GPU, "global_images": B_PER_GPU * world,
-                   "K": K_NBR, "guide_channels": CG, "value_channels": C, "scale": 2,
-                   "levels": [f"{c}^2->{f}^2" for c, f in LEVELS],
-                   "out_mpix_per_step_per_gpu": round(mpix_step, 4),
-                   "l2": "inputs larger than L2 (3.03 GB algorithmic per step), no flush",
-                   "parallelism": f"batch-sharded x{world}, no data-path collective"},
+        "config": workload_config(world),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      # every launch of a step is the attender kernel: achieved = mean launch's
@@ -307,6 +345,8 @@ def run_ours(args, world, rank, local):
         "gpu_launches": len(LEVELS) * args.steps,
         "clocks": clk,
     }
+    if triton is not None:
+        result["triton_reference"] = triton
     if ups is not None:
         result["upsampler"] = ups
     if models is not None:
@@ -317,7 +357,85 @@ def run_ours(args, world, rank, local):
         result["backward"] = bwd
     if cpu is not None:
         result["cpu_baseline"] = cpu
+    result["summary"] = summary(result)
     return result
+
+
+def summary(r):
+    """A short last key: the headline figures of the line, so that a
+    truncated tail of the output still carries them."""
+    def get(*path):
+        x = r
+        for p in path:
+            if not isinstance(x, dict) or p not in x:
+                return None
+            x = x[p]
+        return x
+    return {"n": r["n_gpus"], "attender_Mpix_s": r["value"], "frac": get("roofline", "frac"),
+            "e2e_Mpix_s": get("e2e", "value"), "e2e_copy_frac": get("e2e", "copy_roofline", "e2e_frac"),
+            "triton_ref_Mpix_s": get("triton_reference", "Mpix_s"),
+            "cfg5_img_s": get("upsampler", "img_per_s"),
+            "cfg5_img_s_gather": get("upsampler", "gather", "img_per_s"),
+            "cfg3_img_s": get("upsampler_other_configs", "dinov3_splus16_512_b32_bf16", "img_per_s"),
+            "cfg4_img_s": get("upsampler_other_configs", "sd15_vae_512_b16_fp32", "img_per_s"),
+            "bwd_frac": get("backward", "frac_of_peak_chain")}
+
+
+def run_triton_reference(dev, stream, la, value0, guides, ours_out, ours_ms_step, steps=10):
+    """The reference's own GPU path on the same chain, inputs and weights:
+    _TritonAttenderWrapper (cuDNN conv1 + residual_auto, uplift/fast.py:46-64)
+    around TritonLocalAttender (F.pad replicate copy, cell-tiled kernel for
+    H < 48, NHWC streaming kernel + NCHW copy-back otherwise,
+    uplift/kernels/triton_attender.py:317-400), unmodified from the
+    baseline/_ref install; eager calls as the reference runs them (its
+    module is excluded from compilation), CUDA events, after 3 warm-up
+    chains (Triton JIT + autotune).  Reports its Mpix/s beside this
+    repository's step time, and the normwise difference of the two final
+    outputs (both bf16; different rounding points)."""
+    import copy
+    mods, why = reference_modules("fast", "kernels.triton_attender")
+    if not mods:
+        return {"unavailable": why}
+    fast_mod, ta = mods
+    try:
+        wrapper = fast_mod._TritonAttenderWrapper(copy.deepcopy(la.conv1), la.conv_res,
+                                                  ta.TritonLocalAttender(K_NBR)).to(dev).eval()
+
+        def chain(ev=None):
+            v = value0
+            for i, g in enumerate(guides):
+                if ev is not None:
+                    ev[i][0].record(stream)
+                v = wrapper(g, v)
+                if ev is not None:
+                    ev[i][1].record(stream)
+            return v
+
+        with torch.inference_mode():
+            for _ in range(3):
+                out = chain()
+            torch.cuda.synchronize(dev)
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for _ in range(steps):
+                out = chain()
+            t1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = t0.elapsed_time(t1) / steps
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in guides]
+            chain(ev)
+            torch.cuda.synchronize(dev)
+            lvl = [round(a.elapsed_time(b), 4) for a, b in ev]
+        ref = out.float()
+        err = ((ours_out.float() - ref).abs().max() / ref.abs().max()).item()
+    except Exception as e:  # noqa: BLE001 -- reported in the line
+        return {"unavailable": f"reference Triton path failed: {type(e).__name__}: {e}"[:300]}
+    mpix = out_pixels() / 1e6
+    return {"Mpix_s": round(mpix / (ms / 1e3), 1), "ms_per_step": round(ms, 4), "ms_per_level_eager": lvl,
+            "ours_ms_per_step": round(ours_ms_step, 4), "speedup_ours": round(ms / ours_ms_step, 2),
+            "normwise_diff_vs_ours": round(err, 5),
+            "path": "reference _TritonAttenderWrapper + TritonLocalAttender (baseline/_ref, unmodified), "
+                    "eager, bf16, same inputs and weights"}
 
 
 def run_fp32_configs(dev, stream, peak, reps=20):
@@ -434,10 +552,13 @@ def run_e2e(la, host, dev, stream, world, args, mpix_step):
     compute (two slots of device inputs and pinned host outputs; events order
     the slots).  The timed region spans the first input copy to the last
     output copy."""
-    h_v0 = host["value0"].pin_memory()
-    h_guides = [x.pin_memory() for x in host["guides"]]
-    h_outs = [torch.empty((B_PER_GPU, C, LEVELS[-1][1], LEVELS[-1][1]), dtype=torch.bfloat16,
-                          memory_format=torch.channels_last).pin_memory() for _ in range(2)]
+    # pinned host buffers on the GPU's NUMA node (pages are placed when they
+    # are pinned, by the pinning thread)
+    with numa_local(dev) as numa:
+        h_v0 = host["value0"].pin_memory()
+        h_guides = [x.pin_memory() for x in host["guides"]]
+        h_outs = [torch.empty((B_PER_GPU, C, LEVELS[-1][1], LEVELS[-1][1]), dtype=torch.bfloat16,
+                              memory_format=torch.channels_last).pin_memory() for _ in range(2)]
     h2d = h_v0.numel() * 2 + sum(x.numel() * 2 for x in h_guides)
     d2h = h_outs[0].numel() * 2
     d_v0 = [torch.empty_like(h_v0, device=dev) for _ in range(2)]
@@ -489,14 +610,100 @@ def run_e2e(la, host, dev, stream, world, args, mpix_step):
         torch.cuda.synchronize(dev)
         barrier(world)
     e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / e_steps
-    return {"value": round(world * mpix_step / (e_ms / 1e3), 2), "unit": UNIT,
+    value = world * mpix_step / (e_ms / 1e3)
+    bound = copy_bound(dev, h_v0, h_guides, h_outs[0], world)
+    bound_mpix = world * mpix_step / (bound["both_ms"] / 1e3)
+    bound.update({"Mpix_s": round(bound_mpix, 2), "e2e_frac": round(value / bound_mpix, 4), "numa": numa})
+    return {"value": round(value, 2), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms, 3),
             "api": "uplift_b200.LocalAttender.forward, pinned host buffers",
-            "pipelining": "H2D of step i+1 and D2H of step i-1 overlap step i's compute (3 streams, 2 slots)"}
+            "pipelining": "H2D of step i+1 and D2H of step i-1 overlap step i's compute (3 streams, 2 slots)",
+            "copy_roofline": bound}
+
+
+class numa_local:
+    """Run a block with the calling thread bound to the CPUs of the GPU's
+    NUMA node (from sysfs), so that host memory pinned inside it is placed
+    on that node; the previous affinity is restored after.  Yields a short
+    description (None when sysfs has no answer)."""
+
+    def __init__(self, dev):
+        self.dev = dev
+        self.old = None
+
+    def __enter__(self):
+        try:
+            props = torch.cuda.get_device_properties(self.dev)
+            bdf = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            p = Path("/sys/bus/pci/devices") / bdf
+            node = int((p / "numa_node").read_text().strip())
+            cpus = set()
+            for part in (p / "local_cpulist").read_text().strip().split(","):
+                a, _, b = part.partition("-")
+                cpus.update(range(int(a), int(b or a) + 1))
+            cpus &= os.sched_getaffinity(0)
+            if not cpus:
+                return None
+            self.old = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, cpus)
+            return {"node": node, "cpus": len(cpus), "pci": bdf}
+        except (AttributeError, OSError, ValueError, RuntimeError):
+            return None
+
+    def __exit__(self, *exc):
+        if self.old is not None:
+            os.sched_setaffinity(0, self.old)
+        return False
+
+
+def copy_bound(dev, h_v0, h_guides, h_out, world, reps=5):
+    """The e2e pipeline's copy roofline: the same pinned host buffers copied
+    host->device (level-0 features + four guides) and device->host (final
+    output) with nothing else running, both directions at once on two
+    streams as the pipeline overlaps them, on every rank at the same time;
+    median of `reps`, max over ranks.  Also each direction alone."""
+    d_in = [torch.empty_like(h_v0, device=dev)] + [torch.empty_like(x, device=dev) for x in h_guides]
+    d_out = torch.empty_like(h_out, device=dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    cur = torch.cuda.current_stream(dev)
+
+    def once(do_in, do_out):
+        start, e_in, e_out = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        start.record(cur)
+        if do_in:
+            s_in.wait_event(start)
+            with torch.cuda.stream(s_in):
+                for d, h in zip(d_in, [h_v0] + list(h_guides)):
+                    d.copy_(h, non_blocking=True)
+            e_in.record(s_in)
+            cur.wait_event(e_in)
+        if do_out:
+            s_out.wait_event(start)
+            with torch.cuda.stream(s_out):
+                h_out.copy_(d_out, non_blocking=True)
+            e_out.record(s_out)
+            cur.wait_event(e_out)
+        end = torch.cuda.Event(enable_timing=True)
+        end.record(cur)
+        end.synchronize()
+        return start.elapsed_time(end)
+
+    res = {}
+    for name, a, b in (("both", True, True), ("h2d", True, False), ("d2h", False, True)):
+        once(a, b)
+        barrier(world)
+        ms = statistics.median(once(a, b) for _ in range(reps))
+        res[name + "_ms"] = round(max_over_ranks(ms, world, dev), 3)
+    h2d = sum(x.numel() * x.element_size() for x in [h_v0] + list(h_guides))
+    d2h = h_out.numel() * h_out.element_size()
+    res["h2d_GB_s"] = round(h2d / res["h2d_ms"] / 1e6, 1)
+    res["d2h_GB_s"] = round(d2h / res["d2h_ms"] / 1e6, 1)
+    return res
 
 
 def run_upsampler(dev, stream, world, rank, args, variant="dinov2-s14", img_px=1022, feat_px=73, iters=4,
-                  global_images=64, micro_batch=8, dtype=torch.bfloat16, outsize=None, img_range=(0.0, 1.0)):
+                  global_images=64, micro_batch=8, dtype=torch.bfloat16, outsize=None, img_range=(0.0, 1.0),
+                  gather=False, gather_micro_batch=2, min_ms=400.0):
     """Whole-upsampler throughput, batch-sharded: the `variant`-shaped UPLiFT
     (random init, eval, channels_last) on images img_px^2 in `img_range`
     with backbone features C x feat_px^2 (N(0,1)), iters, final resize to
@@ -504,8 +711,19 @@ def run_upsampler(dev, stream, world, rank, args, variant="dinov2-s14", img_px=1
     contiguous shards, one per rank, each run in micro-batches of
     `micro_batch` images.  Convolutions are cuDNN, the glue between them and
     the attender are this package's kernels.  Inputs are resident on the
-    device (synthetic, seed 1000 + rank); img/s = global images /
-    max-over-ranks time."""
+    device (synthetic, seed 1000 + rank).
+
+    Each micro-batch forward is captured once in a CUDA graph and replayed
+    (the eager figure, with per-launch host overhead, is reported beside it);
+    a pass = every micro-batch of the rank's shard, timed over enough passes
+    to last `min_ms`; img/s = global images / max-over-ranks time.
+
+    `gather` (N > 1): a second timing in which every output also travels to
+    rank 0 (NCCL gather into one preallocated [global, C, H, W] tensor on
+    rank 0 only), micro-batch by micro-batch in `gather_micro_batch`-image
+    pieces so that the transfer of one overlaps the forward of the next
+    (two graph slots; a slot is replayed again only after its gather has
+    read it)."""
     from uplift_b200.configs import get_config
     from uplift_b200.sharding import shard_bounds
     from uplift_b200.uplift import UPLiFT
@@ -528,43 +746,135 @@ def run_upsampler(dev, stream, world, rank, args, variant="dinov2-s14", img_px=1
     img = img.contiguous(memory_format=torch.channels_last)
     feats = feats.contiguous(memory_format=torch.channels_last)
     size = None if outsize is None else [outsize, outsize]
+    n_mb = (mine + mb - 1) // mb
 
-    def one_pass():
-        done, out = 0, None
-        while done < mine:
-            n = min(mb, mine - done)
-            out = fast(img[:n], feats[:n], size)
-            done += n
-        return out
-
-    steps = max(1, min(args.steps, 2))
-    with torch.inference_mode():
-        one_pass()  # warm-up (cuDNN algorithm selection)
-        torch.cuda.synchronize(dev)
+    def timed(fn, passes):
         barrier(world)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(steps):
-            out = one_pass()
+        for _ in range(passes):
+            fn()
         e1.record(stream)
         torch.cuda.synchronize(dev)
         barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
-    if out is not None:
-        assert out.shape[1] == cfg.backbone.channel
-    del fast, model, img, feats, out
+        return max_over_ranks(e0.elapsed_time(e1), world, dev) / passes
+
+    def passes_for(ms_one):  # enough passes for ~min_ms (same count on every rank)
+        return int(max(2, min(50, -(-min_ms // max(ms_one, 1e-3)))))
+
+    with torch.inference_mode():
+        # eager: warm-up (cuDNN algorithm selection), then timed
+        out = fast(img, feats, size)
+        torch.cuda.synchronize(dev)
+
+        def eager_pass():
+            for _ in range(n_mb):
+                fast(img, feats, size)
+        ms_eager = timed(eager_pass, 1)
+        ms_eager = timed(eager_pass, passes_for(ms_eager))
+
+        # CUDA graph of one micro-batch forward, replayed per micro-batch
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fast(img, feats, size)
+        stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_out = fast(img, feats, size)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+
+        def graph_pass():
+            for _ in range(n_mb):
+                graph.replay()
+        ms = timed(graph_pass, 1)
+        passes = passes_for(ms)
+        ms = timed(graph_pass, passes)
+        assert static_out.shape[1] == cfg.backbone.channel
+        out_shape = tuple(static_out.shape[1:])
+        del graph, static_out, out
+
+        gat = None
+        if gather and world > 1:
+            gat = run_gather(fast, dev, stream, world, rank, global_images, mine, lo, img, feats, size,
+                             dtype, out_shape, min(gather_micro_batch, mb), timed, passes_for)
+    del fast, model, img, feats
     torch.cuda.empty_cache()
     dt = {torch.bfloat16: "bf16", torch.float32: "fp32"}[dtype]
     shape = f"{outsize}^2 output" if outsize else "no final resize"
+    res = {"img_per_s": round(global_images / (ms / 1e3), 2), "ms_per_global_batch": round(ms, 2),
+           "img_per_s_eager": round(global_images / (ms_eager / 1e3), 2),
+           "global_images": global_images, "images_per_gpu": mine, "micro_batch": mb, "passes": passes,
+           "scaling": "strong", "timing": "CUDA-graph replay per micro-batch (eager beside it)",
+           "config": f"UPLiFT {variant}, random init, {dt}, img {img_px}^2, feats "
+                     f"{cfg.backbone.channel}x{feat_px}^2, iters={iters}, {shape}; make_fast(compile=False)"}
+    if gat is not None:
+        res["gather"] = gat
+    return res
+
+
+def run_gather(fast, dev, stream, world, rank, global_images, mine, lo, img, feats, size, dtype, out_shape,
+               gmb, timed, passes_for):
+    """Upsampler timing with the final gather of every output to rank 0 (see
+    run_upsampler).  Shards are equal (global batch divisible by the world
+    size), so every rank issues the same gathers in the same order."""
+    import torch.distributed as dist
+    from uplift_b200.sharding import shard_bounds
+    C, H, W = out_shape
+    bounds = [shard_bounds(global_images, r, world) for r in range(world)]
+    if len({hi - lo_ for lo_, hi in bounds}) != 1 or mine % gmb != 0:
+        return {"skipped": "unequal shards"}
+    full = None
+    if rank == 0:
+        full = torch.empty((global_images, C, H, W), dtype=dtype, device=dev, memory_format=torch.channels_last)
+    n_mb = mine // gmb
+    x_img, x_feats = img[:gmb], feats[:gmb]
+    pool = torch.cuda.graph_pool_handle()
+    graphs, outs = [], []
+    for _ in range(2):  # two slots: one is gathered while the other is computed
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fast(x_img, x_feats, size)
+        stream.wait_stream(side)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, pool=pool):
+            outs.append(fast(x_img, x_feats, size))
+        graphs.append(gr)
+    torch.cuda.synchronize(dev)
+
+    def nhwc(t):  # a contiguous view of a channels_last tensor, as NCCL wants it
+        return t.permute(0, 2, 3, 1)
+
+    def gather_pass():
+        pending = [None, None]
+        for j in range(n_mb):
+            sl = j & 1
+            if pending[sl] is not None:
+                pending[sl].wait()  # the stream waits until that gather has read the slot
+            graphs[sl].replay()
+            parts = None
+            if rank == 0:
+                parts = [nhwc(full[lo_ + j * gmb: lo_ + (j + 1) * gmb]) for lo_, _ in bounds]
+            pending[sl] = dist.gather(nhwc(outs[sl]), gather_list=parts, dst=0, async_op=True)
+        for w in pending:
+            if w is not None:
+                w.wait()
+    ms = timed(gather_pass, 1)
+    passes = passes_for(ms)
+    ms = timed(gather_pass, passes)
+    del graphs, outs, full
+    elem = 2 if dtype != torch.float32 else 4
+    into_root = (world - 1) * mine * C * H * W * elem
     return {"img_per_s": round(global_images / (ms / 1e3), 2), "ms_per_global_batch": round(ms, 2),
-            "global_images": global_images, "images_per_gpu": mine, "micro_batch": mb,
-            "scaling": "strong (global batch fixed, sharded over ranks)", "steps": steps,
-            "config": f"UPLiFT {variant}-shaped, random init, {dt}, images {img_px}^2 in {list(img_range)}, "
-                      f"feats {cfg.backbone.channel}x{feat_px}^2, iters={iters}, {shape}; make_fast(compile=False): "
-                      f"BatchNorm folded, channels_last, cuDNN convs (benchmark mode; fused conv+ReLU), conv "
-                      f"epilogues, LayerNorm, resampling and concatenation on the glue kernels, attender fused "
-                      f"kernel"}
+            "passes": passes, "gather_micro_batch": gmb,
+            "bytes_into_rank0_per_batch": into_root,
+            "rank0_ingress_GB_s": round(into_root / (ms / 1e3) / 1e9, 1),
+            "how": "NCCL gather per micro-batch into rank 0's [global, C, H, W] tensor, overlapping the next "
+                   "micro-batch's forward (2 CUDA-graph slots); only rank 0 holds the full batch"}
 
 
 def run_model_configs(dev, stream, world, rank, args):
@@ -594,12 +904,27 @@ def cpu_sample_inputs(host, seed=1):
     return [(host["guides"][i][:1].contiguous(), vals[i]) for i in range(len(LEVELS))]
 
 
-def cpu_band_step(la, inputs, band):
-    """Reference algorithm (the oracle's restatement of the non-fast
-    LocalAttender with torch CPU ops, parallel pooling, bf16) on band `band`
-    of 8 horizontal bands of every level of one image; each band is computed
-    with its +-pn halo rows, so its output equals the whole-image result.
-    Returns the output pixels produced."""
+def reference_attender(la):
+    """The reference's own LocalAttender (uplift/uplift.py:740-847, from the
+    baseline/_ref install) carrying the weights of `la`, in bf16; (None,
+    reason) when the install is absent."""
+    mods, why = reference_modules("uplift")
+    if not mods:
+        return None, why
+    ref = mods[0].LocalAttender(CG, K_NBR).to(torch.bfloat16).eval()
+    with torch.no_grad():
+        ref.conv1.weight.copy_(la.conv1.weight.detach().cpu())
+        ref.conv1.bias.copy_(la.conv1.bias.detach().cpu())
+    return ref, None
+
+
+def cpu_band_step(la, inputs, band, ref=None):
+    """Band `band` of 8 horizontal bands of every level of one image through
+    the CPU implementation of the path: the reference's own LocalAttender
+    when `ref` is given, else the oracle's restatement of it (torch CPU ops,
+    same op order, parallel pooling, bf16).  Each band is computed with its
+    +-pn halo rows, so its output equals the whole-image result.  Returns the
+    output pixels produced."""
     from oracle import local_attender_oracle as lao
     w = la.conv1.weight.detach().cpu().reshape(K_NBR, CG)
     b = la.conv1.bias.detach().cpu()
@@ -610,9 +935,21 @@ def cpu_band_step(la, inputs, band):
             H = value.shape[2]
             h0, h1 = band * H // 8, (band + 1) * H // 8
             lo, hi = max(0, h0 - pn), min(H, h1 + pn)
-            lao.local_attender(guide[:, :, 2 * lo:2 * hi], value[:, :, lo:hi], w, b, K=K_NBR)
+            g, v = guide[:, :, 2 * lo:2 * hi], value[:, :, lo:hi]
+            if ref is not None:
+                ref(g, v)
+            else:
+                lao.local_attender(g, v, w, b, K=K_NBR)
             pix += 2 * (h1 - h0) * guide.shape[3]
     return pix
+
+
+def cpu_impl(la):
+    """(reference module or None, kind, description) of the CPU path timed."""
+    ref, why = reference_attender(la)
+    if ref is not None:
+        return ref, "reference", "the reference's LocalAttender.forward (uplift/uplift.py:801-847, parallel pooling)"
+    return None, "port", f"oracle restatement of the reference (torch CPU ops; {why})"
 
 
 def cpu_baseline(la, host, min_seconds=10.0):
@@ -620,49 +957,49 @@ def cpu_baseline(la, host, min_seconds=10.0):
     repeated until about `min_seconds` of CPU work, all host threads."""
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
+    ref, kind, what = cpu_impl(la)
     inputs = cpu_sample_inputs(host)
-    cpu_band_step(la, inputs, 4)  # warm-up
+    cpu_band_step(la, inputs, 4, ref)  # warm-up
     t = time.perf_counter()
     pix, n = 0, 0
     while True:
-        pix += cpu_band_step(la, inputs, n % 8)
+        pix += cpu_band_step(la, inputs, n % 8, ref)
         n += 1
         sec = time.perf_counter() - t
         if n >= 8 and sec >= min_seconds:
             break
-    return {"value": round(pix / 1e6 / sec, 4), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{n} bands of 1/8 image rows x 4 attender levels (= {n / 8:.2f} images of "
-                      f"the 448px iters=4 chain, {pix} output px) in {sec:.1f} s; reference "
-                      "algorithm restated with torch CPU ops (parallel pooling), bf16"}
+    return {"value": round(pix / 1e6 / sec, 4), "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{n} bands of 1/8 image rows x 4 attender levels (= {n / 8:.2f} images of the "
+                      f"448px iters=4 chain, {pix} output px) in {sec:.1f} s; {what}, bf16"}
 
 
 def run_reference(args, world, rank):
-    """The reference's CPU implementation of the path (oracle port), rank 0.
-    One step = one 1/8-row band of one image through the 4 attender levels."""
+    """The reference's CPU implementation of the path, rank 0 only: each step
+    = one 1/8-row band of one image through the 4 attender levels (bands
+    cycle through the image)."""
     if rank != 0:
         return None
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     la, host = make_inputs(torch.device("cpu"), seed=0)
+    ref, kind, what = cpu_impl(la)
     inputs = cpu_sample_inputs(host)
     for i in range(min(args.warmup, 2)):
-        cpu_band_step(la, inputs, i % 8)
+        cpu_band_step(la, inputs, i % 8, ref)
     pix = 0
     t = time.perf_counter()
     for i in range(args.steps):
-        pix += cpu_band_step(la, inputs, i % 8)
+        pix += cpu_band_step(la, inputs, i % 8, ref)
     sec = time.perf_counter() - t
     value = pix / 1e6 / sec
     sample = (f"per step 1/8 of the rows of one image through the 4 attender levels "
-              f"({pix // max(args.steps, 1)} output px avg), reference algorithm restated with torch "
-              "CPU ops (parallel pooling), bf16")
+              f"({pix // max(args.steps, 1)} output px avg); {what}, bf16")
     return {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(sec * 1e3 / max(args.steps, 1), 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "dinov2-s14-448-iters4 Local Attender chain", "K": K_NBR,
-                       "guide_channels": CG, "value_channels": C, "scale": 2},
-            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
+            "config": workload_config(world),
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": kind,
                              "sample": sample},
             "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -683,6 +1020,8 @@ def main():
     ap.add_argument("--only-fp32", action="store_true",
                     help="run only the fp32 attender configurations (profiling captures)")
     ap.add_argument("--no-backward", action="store_true", help="skip the attender backward pass")
+    ap.add_argument("--no-triton", action="store_true", help="skip timing the reference's Triton path")
+    ap.add_argument("--no-gather", action="store_true", help="skip the upsampler timing with the gather to rank 0")
     ap.add_argument("--only-backward", action="store_true",
                     help="run only the attender backward pass (profiling captures)")
     ap.add_argument("--only-upsampler", action="store_true",
@@ -710,7 +1049,8 @@ def main():
             res = {"backward": run_backward(dev, torch.cuda.current_stream(dev), load_peaks()[0], B_PER_GPU)}
         elif args.only_upsampler:
             dev = torch.device("cuda", local)
-            res = {"upsampler": run_upsampler(dev, torch.cuda.current_stream(dev), world, rank, args, outsize=1022)}
+            res = {"upsampler": run_upsampler(dev, torch.cuda.current_stream(dev), world, rank, args, outsize=1022,
+                                              gather=not args.no_gather)}
         else:
             res = run_ours(args, world, rank, local)
         if rank == 0:

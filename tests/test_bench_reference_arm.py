@@ -1,6 +1,8 @@
-"""The reference arm of bench.py (`--impl reference`: the reference algorithm
-restated on the host CPU, the one arm that needs no GPU) runs and prints the
-JSON line of the benchmark contract."""
+"""The reference arm of bench.py (`--impl reference`: the reference's CPU
+implementation of the path on the host cores -- its own LocalAttender from
+the baseline/_ref install when present, else the oracle's restatement --
+the one arm that needs no GPU) runs and prints the JSON line of the
+benchmark contract, with the same `config` as the repository's arm."""
 import json
 import subprocess
 import sys
@@ -19,6 +21,11 @@ def test_reference_arm_json_line():
                 "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
         assert key in d, key
     assert d["impl"] == "reference" and d["value"] > 0 and d["unit"] == "Mpix/s"
-    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    installed = (ROOT / "baseline" / "_ref" / "uplift" / "uplift.py").exists()
+    assert d["cpu_baseline"]["kind"] == ("reference" if installed else "port")
+    assert d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert d["config"]["workload"].startswith("dinov2-s14-448-iters4")
+    sys.path.insert(0, str(ROOT))
+    import bench
+    assert d["config"] == bench.workload_config(1)  # the repository arm's config object

@@ -41,10 +41,15 @@ def _worker(rank, world, port, n, fail_rank, q):
         if rank == fail_rank:
             raise RuntimeError("injected failure before the gather")
         got = gather_to_rank0(local, n)
+        # channels_last images travel as their NHWC storage
+        imgs = torch.arange(n * 4 * 3 * 5, dtype=torch.float32).reshape(n, 4, 3, 5)
+        imgs = imgs.contiguous(memory_format=torch.channels_last)
+        got_cl = gather_to_rank0(shard(imgs, rank, world) + 1.0, n)
         if rank == 0:
-            q.put(("ok", torch.equal(got, full * 2.0)))
+            q.put(("ok", torch.equal(got, full * 2.0) and torch.equal(got_cl, imgs + 1.0)
+                   and got_cl.is_contiguous(memory_format=torch.channels_last)))
         else:
-            q.put(("ok", got is None))
+            q.put(("ok", got is None and got_cl is None))
     except Exception as e:  # noqa: BLE001 - reported to the parent
         q.put(("err", f"rank {rank}: {type(e).__name__}"))
     finally:
