@@ -47,6 +47,9 @@ extern "C" {
 #define UPLIFT_LA_ERR_OFFSETS    4  /* |offset| > pn, or pn out of range    */
 #define UPLIFT_LA_ERR_CUDA       5  /* a CUDA runtime call or launch failed */
 #define UPLIFT_LA_ERR_NO_DEVICE  6  /* no usable sm_100 device              */
+#define UPLIFT_LA_ERR_UNSUPPORTED 7 /* no fused kernel applies; nothing was
+                                       launched (the caller runs the steps
+                                       separately)                          */
 
 /* largest neighbourhood and padding the kernels accept */
 #define UPLIFT_LA_MAX_K  25
@@ -79,6 +82,32 @@ int uplift_la_forward(const void* guide, const int64_t guide_strides[4],
                       int B, int Cg, int C, int H, int W, int I, int K,
                       const int8_t* offsets, int pn, int conv_res,
                       int dtype, int hardmax, void* stream);
+
+/*
+ * uplift_la_forward followed by the fast path's final resize, in one launch:
+ * out [B, C, Ho, Wo] = F.interpolate(attender output, size=(Ho, Wo),
+ * mode="bilinear", align_corners=False), the resize of _OptimizedUPLiFT's
+ * last step (uplift/fast.py:218-220).  The attender output itself is never
+ * stored: each output tile is resampled in shared memory from the attender
+ * values of its tile rounded to the storage type, as the stored tensor would
+ * hold them, then interpolated in fp32 with PyTorch's source-index formula
+ * (results equal the two separate steps up to the fp32 contraction order,
+ * <= 1 storage ulp).  Applies to the tensor-core kernel's problems (bf16 /
+ * fp16, I = 2, Cg = 64, C a multiple of 64 up to 384) whose output is 7/8 of
+ * the attender output in both dimensions -- 1168 -> 1022 and 512 -> 448 in
+ * the DINOv2 upsampler -- with the attender output a whole number of 8 x 16
+ * tiles; then every 8 x 16 attender tile maps onto exactly 7 x 14 output
+ * pixels and no tile needs another's values.  Otherwise returns
+ * UPLIFT_LA_ERR_UNSUPPORTED and launches nothing.  Other arguments as for
+ * uplift_la_forward.  No single reference counterpart (it fuses two).
+ */
+int uplift_la_forward_resized(const void* guide, const int64_t guide_strides[4],
+                              const void* value, const int64_t value_strides[4],
+                              const float* weight, const float* bias,
+                              void* out, const int64_t out_strides[4],
+                              int B, int Cg, int C, int H, int W, int I, int K,
+                              const int8_t* offsets, int pn, int conv_res,
+                              int dtype, int hardmax, int Ho, int Wo, void* stream);
 
 /*
  * Softmax-pool from pre-projected logits: the same kernel with the
@@ -175,6 +204,7 @@ int uplift_la_set_kernel_policy(int policy);
 #define UPLIFT_LA_KERNEL_TENSOR_CORE 2
 #define UPLIFT_LA_KERNEL_SIMT_STAGED 3  /* CUDA-core kernel, guide staged in shared memory */
 #define UPLIFT_LA_KERNEL_TENSOR_CORE_WIDE 4  /* fp32, wide guide: split-bf16 tensor-core projection */
+#define UPLIFT_LA_KERNEL_TENSOR_CORE_RESIZE 5  /* tensor-core kernel with the fused final resize */
 int uplift_la_last_kernel(void);
 
 /* Device status word of the tensor-core kernels: 0 when every launch so far

@@ -98,7 +98,7 @@ def test_fast_executor_matches_plain_all_variants(variant, cuda_lib, monkeypatch
     the reference)."""
     cfg = get_config(variant)
     torch.manual_seed(0)
-    m = U.UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift).eval().to(DEV)
+    m = U.UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift, allow_tf32=False).eval().to(DEV)
     m.enable_iterative(2)
     g = torch.Generator().manual_seed(5)
     side = 64 if variant == "sd15-vae" else 112

@@ -14,7 +14,7 @@ from pathlib import Path
 from . import build as _build
 
 F32, BF16, F16 = 0, 1, 2
-OK, ERR_ARG, ERR_SHAPE, ERR_LAYOUT, ERR_OFFSETS, ERR_CUDA, ERR_NO_DEVICE = range(7)
+OK, ERR_ARG, ERR_SHAPE, ERR_LAYOUT, ERR_OFFSETS, ERR_CUDA, ERR_NO_DEVICE, ERR_UNSUPPORTED = range(8)
 MAX_K = 25
 MAX_PN = 4
 NOALLOC_MAX_PROBS = 8 * 1024 * 1024  # floats, UPLIFT_LA_NOALLOC_MAX_PROBS
@@ -22,6 +22,7 @@ NOALLOC_MAX_PROBS = 8 * 1024 * 1024  # floats, UPLIFT_LA_NOALLOC_MAX_PROBS
 # every symbol include/uplift_la.h declares
 EXPORTED = (
     "uplift_la_forward",
+    "uplift_la_forward_resized",
     "uplift_la_pool",
     "uplift_la_last_error",
     "uplift_la_status_string",
@@ -42,6 +43,7 @@ EXPORTED = (
 )
 POLICY_AUTO, POLICY_SIMT, POLICY_TENSOR_CORE = 0, 1, 2
 KERNEL_SIMT, KERNEL_TENSOR_CORE, KERNEL_SIMT_STAGED, KERNEL_TENSOR_CORE_WIDE = 1, 2, 3, 4
+KERNEL_TENSOR_CORE_RESIZE = 5
 KERNELS_CUDA_CORE = (KERNEL_SIMT, KERNEL_SIMT_STAGED)
 
 _lib = None
@@ -78,6 +80,9 @@ def load(build_if_missing: bool = False):
         lib.uplift_la_forward.restype = i
         lib.uplift_la_forward.argtypes = [vp, i64p, vp, i64p, fp, fp, vp, i64p,
                                           i, i, i, i, i, i, i, i8p, i, i, i, i, vp]
+        lib.uplift_la_forward_resized.restype = i
+        lib.uplift_la_forward_resized.argtypes = [vp, i64p, vp, i64p, fp, fp, vp, i64p,
+                                                  i, i, i, i, i, i, i, i8p, i, i, i, i, i, i, vp]
         lib.uplift_la_pool.restype = i
         lib.uplift_la_pool.argtypes = [vp, i64p, vp, i64p, vp, i64p,
                                        i, i, i, i, i, i, i8p, i, i, i, vp]

@@ -154,7 +154,14 @@ class AttenderWrapper(nn.Module):
         self._proj_key = None
         self._proj = None
 
-    def forward(self, guide, value, hardmax=False):
+    def forward(self, guide, value, hardmax=False, size=None):
+        """`size` (an addition to the reference's wrapper): the output also
+        goes through the fast path's final bilinear resize to `size`
+        (uplift/fast.py:218-220), fused into the attender launch where the
+        tensor-core kernel allows it."""
         w, b = _fp32_projection(self, self.conv1, self.num_connected)
+        if size is not None:
+            return ops.local_attender_resized(guide, value, w, b, self.offsets, self.pn, size,
+                                              conv_res=self.conv_res, hardmax=hardmax)
         return ops.local_attender(guide, value, w, b, self.offsets, self.pn,
                                   conv_res=self.conv_res, hardmax=hardmax)

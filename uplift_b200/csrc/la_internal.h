@@ -19,10 +19,17 @@ struct TcArgs {
   int B, Cg, C, H, W, K, pn;
   int conv_res, hardmax, dtype;
   const int8_t* offsets;  // host [K][2]
+  // fused final resize: out is [B, Ho, Wo, C], the bilinear
+  // (align_corners=False) resize of the attender output; 0 = no resize
+  int Ho = 0, Wo = 0;
 };
 
 // True when the tensor-core kernel supports the problem (sizes, alignment).
 bool tc_eligible(const TcArgs& a, const char** why);
+
+// True when the tensor-core kernel can also apply the final bilinear resize
+// to a.Ho x a.Wo (see la_tc.cu); checked on top of tc_eligible.
+bool tc_resize_eligible(const TcArgs& a, const char** why);
 
 // Launch the tensor-core kernel; returns a UPLIFT_LA_* status.
 int tc_launch(const TcArgs& a, cudaStream_t stream);

@@ -92,6 +92,15 @@ constexpr int kOffBar = kOffA2 + 2 * kA2Bytes;
 constexpr int kNumBars = 2 + 2 + kNU + kNU + 2 + 2 + 2 + 2 + 2 + 2 + 1;
 constexpr int kWarpStage = 32 * 128;         // 4 KB: one epilogue warp's 32 px x 64 ch
 constexpr int kOffMisc = kOffBar + kNumBars * 8;   // tmem slot, abort flag
+// Fused final resize (RS kernels): each epilogue warpgroup uses its half of
+// the staging region for one 8 x 16-pixel, 64-channel slice of the tile in
+// storage precision (T) and the 7 x 14 resized pixels made from it (O,
+// laid out as the TMA store box {64, 14, 7} with the 128-byte swizzle).
+constexpr int kRsHalfBytes = 2 * kStageBytes;           // 32 KB per warpgroup
+constexpr int kRsTileBytes = kM * 128;                  // T: 16 KB
+constexpr int kRsOutY = 7, kRsOutX = 14;                // resized pixels per tile
+constexpr int kRsOutBytes = kRsOutY * kRsOutX * 128;    // O: 12.25 KB (1024-aligned start)
+static_assert(kRsTileBytes + kRsOutBytes + 16 <= kRsHalfBytes, "resize staging exceeds the half region");
 constexpr int kOffBias = kOffMisc + 16;
 constexpr int kSmemBytes = kOffBias + kLogN * 4 + 1024;  // + base alignment slack
 
@@ -110,6 +119,10 @@ struct Params {
   uint64_t timeout_ns;  // limit of every mbarrier wait
   unsigned int* host_status;  // host-visible status word or null
   int test_fault;       // 1: the guide producer issues no loads (tests the timeout path)
+  // fused final resize (RS kernels): the attender output [2H, 2W] is never
+  // stored; omap describes the resized output [Ho, Wo] (box {64, 14, 7}).
+  int Hi, Wi;           // attender output size (2H, 2W)
+  float scale_h, scale_w;  // Hi / Ho, Wi / Wo (align_corners=False)
 };
 
 // Bounded mbarrier wait recording expiries in this kernel's status word.
@@ -154,7 +167,7 @@ __device__ __forceinline__ TileXY tile_of(const Params& p, int t) {
   return r;
 }
 
-template <typename T, int K>
+template <typename T, int K, bool RS>
 __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constant__ Params p) {
   using S = Store<T>;
   extern __shared__ uint8_t smem_raw[];
@@ -445,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       __syncwarp();
       if (lane == 0) mbar_arrive(&a2_full[s]);
     }
-  } else {
+  } else if constexpr (!RS) {
     // ------------------------------------------------------------ epilogue
     // two warpgroups, one per accumulator half: warps 10-13 drain half 0,
     // warps 14-17 half 1.  Each warp owns TMEM lanes 32q..32q+31 = output
@@ -495,6 +508,129 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       }
     }
     if (lane == 0) bulk_wait_all();
+  } else {
+    // ------------------------------------------------- epilogue + resize
+    // The attender output is resampled before it is stored (the bilinear
+    // F.interpolate, align_corners=False, of the fast path's final resize).
+    // The resize maps 8 input rows / 16 input columns onto exactly 7 / 14
+    // output rows / columns (host-checked with the same source-index
+    // formula), so a tile's output pixels depend on that tile alone.  Per
+    // 64-channel chunk the warpgroup writes the tile in storage precision
+    // (rounded as the stored attender output would be) to T, resamples it
+    // to O in fp32 and stores O with one TMA box.  Warps synchronise with
+    // named barriers: one thread waits on the accumulator barrier and
+    // shares the outcome, so all 128 threads always take the same path.
+    const int q = warp & 3;
+    const int h = (warp - 10) >> 2;
+    const int t = tid - (10 + 4 * h) * 32;  // thread in the warpgroup
+    const bool leader = t == 0;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+    uint8_t* sT = sStage + h * kRsHalfBytes;
+    uint8_t* sO = sT + kRsTileBytes;
+    volatile int* go = reinterpret_cast<volatile int*>(sO + kRsOutBytes);
+    const int bar_t = 1 + h, bar_o = 3 + h;
+    const int oc = t >> 3;  // output column of the tile (< 14) this thread resamples
+    const int cg = t & 7;   // its 16-byte channel group
+    const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
+    for (int n = 0; n < local_tiles && j0 < j1; ++n) {
+      const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+      if (leader) *go = mbar_wait(&out_full[h], n & 1, abort_flag, 4, tmo) ? 1 : 0;
+      named_bar(bar_t, 128);
+      if (*go == 0) break;
+      tc_fence_after();
+      // source columns of this thread's output column (same for every row)
+      const int ox = kRsOutX * (tl.cx0 / kCellsX) + oc;
+      int x0 = 0, xp = 0;
+      float lx0 = 0.f, lx1 = 0.f;
+      src_coord_bilinear(ox, p.scale_w, p.Wi, x0, xp, lx0, lx1);
+      const int xa = min(max(x0 - 2 * tl.cx0, 0), 15), xb = min(xa + xp, 15);
+      for (int j = j0; j < j1; ++j) {
+        // T row of this lane's pixel (TMEM lane = pixel of the tile), read
+        // from TMEM 32 columns at a time
+        uint8_t* trow = sT + (32 * q + lane) * 128;
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          uint32_t r[32];
+          tc_ld32(lane_base + kChunk * j + 32 * part, r);
+          tc_wait_ld();
+          if (part == 1 && j + 1 == j1) {  // last TMEM read of this half is complete
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&out_empty[h]);
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t* src = r + 8 * c;
+            uint4 w;
+            w.x = S::pack(__uint_as_float(src[0]), __uint_as_float(src[1]));
+            w.y = S::pack(__uint_as_float(src[2]), __uint_as_float(src[3]));
+            w.z = S::pack(__uint_as_float(src[4]), __uint_as_float(src[5]));
+            w.w = S::pack(__uint_as_float(src[6]), __uint_as_float(src[7]));
+            const int cc = 4 * part + c;
+            *reinterpret_cast<uint4*>(trow + ((cc ^ (lane & 7)) << 4)) = w;
+          }
+        }
+        if (leader) bulk_wait_read0();  // the previous chunk's store has read O
+        named_bar(bar_t, 128);
+        if (oc < kRsOutX) {
+          // sweep the 7 output rows: the horizontal interpolation of each
+          // source row is computed once and reused by the next output row
+          float ha[8], hb[8];
+          int ra = -1, rb = -1;
+          auto horiz = [&](int yl, float* dst) {
+            const int pa = yl * 16 + xa, pb = yl * 16 + xb;
+            const uint4 va = *reinterpret_cast<const uint4*>(sT + pa * 128 + ((cg ^ (pa & 7)) << 4));
+            const uint4 vb = *reinterpret_cast<const uint4*>(sT + pb * 128 + ((cg ^ (pb & 7)) << 4));
+            const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float a = S::from_bits((uint16_t)(wa[e >> 1] >> ((e & 1) * 16)));
+              const float b = S::from_bits((uint16_t)(wb[e >> 1] >> ((e & 1) * 16)));
+              dst[e] = lx0 * a + lx1 * b;
+            }
+          };
+          for (int ry = 0; ry < kRsOutY; ++ry) {
+            const int oy = kRsOutY * (tl.cy0 / kCellsY) + ry;
+            int y0, yp;
+            float ly0, ly1;
+            src_coord_bilinear(oy, p.scale_h, p.Hi, y0, yp, ly0, ly1);
+            const int ya = min(max(y0 - 2 * tl.cy0, 0), 7), yb = min(ya + yp, 7);
+            if (ya != ra) {
+              if (ya == rb) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ha[e] = hb[e];
+              } else {
+                horiz(ya, ha);
+              }
+              ra = ya;
+            }
+            if (yb != rb) {
+              if (yb == ra) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) hb[e] = ha[e];
+              } else {
+                horiz(yb, hb);
+              }
+              rb = yb;
+            }
+            uint4 w;
+            w.x = S::pack(ly0 * ha[0] + ly1 * hb[0], ly0 * ha[1] + ly1 * hb[1]);
+            w.y = S::pack(ly0 * ha[2] + ly1 * hb[2], ly0 * ha[3] + ly1 * hb[3]);
+            w.z = S::pack(ly0 * ha[4] + ly1 * hb[4], ly0 * ha[5] + ly1 * hb[5]);
+            w.w = S::pack(ly0 * ha[6] + ly1 * hb[6], ly0 * ha[7] + ly1 * hb[7]);
+            const int orow = ry * kRsOutX + oc;
+            *reinterpret_cast<uint4*>(sO + orow * 128 + ((cg ^ (orow & 7)) << 4)) = w;
+          }
+        }
+        fence_proxy_async();
+        named_bar(bar_o, 128);
+        if (leader) {
+          tma_store(&p.omap, sO, j * kChunk, kRsOutX * (tl.cx0 / kCellsX), kRsOutY * (tl.cy0 / kCellsY), tl.b);
+          bulk_commit();
+        }
+      }
+    }
+    if (leader) bulk_wait_all();
   }
 
   // ---------------------------------------------------------------- teardown
@@ -543,9 +679,9 @@ int tc_make_map(CUtensorMap* map, CUtensorMapDataType dt, int es, const void* ba
 
 namespace tc {
 
-template <typename T, int K>
+template <typename T, int K, bool RS>
 int launch_t(const Params& p, int dev, int grid, cudaStream_t stream) {
-  auto fn = la_tc_kernel<T, K>;
+  auto fn = la_tc_kernel<T, K, RS>;
   // the shared-memory opt-in is per function and device; set it once (two
   // threads racing here both set the same value, which is harmless)
   static std::atomic<bool> configured[64] = {};
@@ -570,14 +706,14 @@ int launch_t(const Params& p, int dev, int grid, cudaStream_t stream) {
   return UPLIFT_LA_OK;
 }
 
-template <typename T>
+template <typename T, bool RS>
 int launch_k(const Params& p, int K, int dev, int grid, cudaStream_t stream) {
   switch (K) {
-    case 5: return launch_t<T, 5>(p, dev, grid, stream);
-    case 9: return launch_t<T, 9>(p, dev, grid, stream);
-    case 13: return launch_t<T, 13>(p, dev, grid, stream);
-    case 17: return launch_t<T, 17>(p, dev, grid, stream);
-    case 25: return launch_t<T, 25>(p, dev, grid, stream);
+    case 5: return launch_t<T, 5, RS>(p, dev, grid, stream);
+    case 9: return launch_t<T, 9, RS>(p, dev, grid, stream);
+    case 13: return launch_t<T, 13, RS>(p, dev, grid, stream);
+    case 17: return launch_t<T, 17, RS>(p, dev, grid, stream);
+    case 25: return launch_t<T, 25, RS>(p, dev, grid, stream);
     default: return fail(UPLIFT_LA_ERR_SHAPE, "K=%d unsupported", K);
   }
 }
@@ -630,15 +766,52 @@ bool tc_eligible(const TcArgs& a, const char** why) {
   return true;
 }
 
+bool tc_resize_eligible(const TcArgs& a, const char** why) {
+  auto no = [&](const char* m) { if (why) *why = m; return false; };
+  using namespace tc;
+  const int Hi = 2 * a.H, Wi = 2 * a.W;
+  if (a.Ho < 1 || a.Wo < 1) return no("empty output size");
+  // tiles of 8 x 16 attender pixels become tiles of 7 x 14 output pixels
+  if ((int64_t)a.Ho * 8 != (int64_t)Hi * kRsOutY || (int64_t)a.Wo * 16 != (int64_t)Wi * kRsOutX)
+    return no("output size is not 7/8 of the attender output in both dimensions");
+  if (a.H % kCellsY != 0 || a.W % kCellsX != 0) return no("attender output not a whole number of 8 x 16 tiles");
+  // every output row / column must read its two source rows / columns from
+  // the 8 / 16 of its own tile (PyTorch's source-index formula, fp32)
+  const float sh = (float)Hi / (float)a.Ho, sw = (float)Wi / (float)a.Wo;
+  for (int d = 0; d < a.Ho; ++d) {
+    int i0, ip;
+    float l0, l1;
+    src_coord_bilinear(d, sh, Hi, i0, ip, l0, l1);
+    const int base = (d / kRsOutY) * 2 * kCellsY;
+    if (i0 < base || i0 + ip > base + 2 * kCellsY - 1) return no("a resized row reads outside its tile");
+  }
+  for (int d = 0; d < a.Wo; ++d) {
+    int i0, ip;
+    float l0, l1;
+    src_coord_bilinear(d, sw, Wi, i0, ip, l0, l1);
+    const int base = (d / kRsOutX) * 2 * kCellsX;
+    if (i0 < base || i0 + ip > base + 2 * kCellsX - 1) return no("a resized column reads outside its tile");
+  }
+  return true;
+}
+
 int tc_launch(const TcArgs& a, cudaStream_t stream) {
   using namespace tc;
   Params p;
   memset(&p, 0, sizeof(p));
+  const bool rs = a.Ho > 0;
   const CUtensorMapDataType dt = a.dtype == UPLIFT_LA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   int rc = tc_make_map(&p.gmap, dt, 2, a.guide, a.Cg, 2 * a.W, 2 * a.H, a.B, a.g_w, a.g_h, a.g_b, 64, 16, 8);
   if (rc == UPLIFT_LA_OK) rc = tc_make_map(&p.vmap, dt, 2, a.value, a.C, a.W, a.H, a.B, a.v_w, a.v_h, a.v_b, 64, kWinX, 8);
-  if (rc == UPLIFT_LA_OK) rc = tc_make_map(&p.omap, dt, 2, a.out, a.C, 2 * a.W, 2 * a.H, a.B, a.o_w, a.o_h, a.o_b, 64, 16, 2);
+  if (rc == UPLIFT_LA_OK) {
+    rc = rs ? tc_make_map(&p.omap, dt, 2, a.out, a.C, a.Wo, a.Ho, a.B, a.o_w, a.o_h, a.o_b, 64, kRsOutX, kRsOutY)
+            : tc_make_map(&p.omap, dt, 2, a.out, a.C, 2 * a.W, 2 * a.H, a.B, a.o_w, a.o_h, a.o_b, 64, 16, 2);
+  }
   if (rc != UPLIFT_LA_OK) return rc;
+  p.Hi = 2 * a.H;
+  p.Wi = 2 * a.W;
+  p.scale_h = rs ? (float)p.Hi / (float)a.Ho : 0.f;
+  p.scale_w = rs ? (float)p.Wi / (float)a.Wo : 0.f;
   p.weight = a.weight;
   p.bias = a.bias;
   int margin = 0;
@@ -670,8 +843,11 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
     if (dev >= 0 && dev < 64) sm_count[dev].store(sms, std::memory_order_relaxed);
   }
   const int grid = (int)std::min<int64_t>(nt, std::max(sms, 1));
-  return a.dtype == UPLIFT_LA_BF16 ? launch_k<__nv_bfloat16>(p, a.K, dev, grid, stream)
-                                   : launch_k<__half>(p, a.K, dev, grid, stream);
+  if (rs)
+    return a.dtype == UPLIFT_LA_BF16 ? launch_k<__nv_bfloat16, true>(p, a.K, dev, grid, stream)
+                                     : launch_k<__half, true>(p, a.K, dev, grid, stream);
+  return a.dtype == UPLIFT_LA_BF16 ? launch_k<__nv_bfloat16, false>(p, a.K, dev, grid, stream)
+                                   : launch_k<__half, false>(p, a.K, dev, grid, stream);
 }
 
 }  // namespace ula

@@ -92,7 +92,23 @@ __device__ __forceinline__ void tma_store(const CUtensorMap* map, const void* sr
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Source index and weights of output coordinate d of a bilinear resize
+// with align_corners=False (PyTorch's area_pixel_compute_source_index and
+// the upsample_bilinear2d weights; `scale` = in / out as fp32): source
+// (d + 0.5) * scale - 0.5 clamped at 0, i0 = its integer part, ip = 1 unless
+// i0 is the last index, weights l0 = 1 - l1 on i0 and l1 on i0 + ip.
+__host__ __device__ __forceinline__ void src_coord_bilinear(int d, float scale, int in, int& i0, int& ip, float& l0,
+                                                           float& l1) {
+  float s = scale * ((float)d + 0.5f) - 0.5f;
+  if (s < 0.f) s = 0.f;
+  i0 = (int)s;
+  ip = (i0 < in - 1) ? 1 : 0;
+  l1 = s - (float)i0;
+  l0 = 1.f - l1;
+}
 __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

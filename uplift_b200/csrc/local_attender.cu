@@ -281,6 +281,59 @@ int uplift_la_forward(const void* guide, const int64_t guide_strides[4],
   return rc;
 }
 
+int uplift_la_forward_resized(const void* guide, const int64_t guide_strides[4],
+                              const void* value, const int64_t value_strides[4],
+                              const float* weight, const float* bias,
+                              void* out, const int64_t out_strides[4],
+                              int B, int Cg, int C, int H, int W, int I, int K,
+                              const int8_t* offsets, int pn, int conv_res,
+                              int dtype, int hardmax, int Ho, int Wo, void* stream) {
+  using namespace ula;
+  if (dtype != UPLIFT_LA_F32 && dtype != UPLIFT_LA_BF16 && dtype != UPLIFT_LA_F16)
+    return fail(UPLIFT_LA_ERR_ARG, "unknown dtype %d", dtype);
+  if (guide_strides == nullptr || value_strides == nullptr || out_strides == nullptr || offsets == nullptr)
+    return fail(UPLIFT_LA_ERR_ARG, "null stride or offset array");
+  if (B < 0 || Cg < 1 || C < 1 || H < 0 || W < 0 || I < 1 || Ho < 1 || Wo < 1)
+    return fail(UPLIFT_LA_ERR_SHAPE, "bad sizes B=%d Cg=%d C=%d H=%d W=%d I=%d Ho=%d Wo=%d", B, Cg, C, H, W, I, Ho,
+                Wo);
+  if (K < 1 || K > kMaxK) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d out of range", K);
+  if (pn < 0 || pn > UPLIFT_LA_MAX_PN) return fail(UPLIFT_LA_ERR_OFFSETS, "pn=%d out of range", pn);
+  for (int k = 0; k < K; ++k) {
+    const int dy = offsets[2 * k], dx = offsets[2 * k + 1];
+    if (dy < -pn || dy > pn || dx < -pn || dx > pn)
+      return fail(UPLIFT_LA_ERR_OFFSETS, "offset %d = (%d, %d) exceeds pn=%d", k, dy, dx, pn);
+  }
+  if (guide_strides[1] != 1 || value_strides[1] != 1 || out_strides[1] != 1)
+    return fail(UPLIFT_LA_ERR_LAYOUT, "guide, value and out need channel stride 1 (channels_last)");
+  if (B == 0) return UPLIFT_LA_OK;
+  if (H == 0 || W == 0) return fail(UPLIFT_LA_ERR_SHAPE, "empty value map with a %dx%d output", Ho, Wo);
+  if (guide == nullptr || value == nullptr || weight == nullptr || out == nullptr)
+    return fail(UPLIFT_LA_ERR_ARG, "null tensor pointer");
+  if (__atomic_load_n(&g_policy, __ATOMIC_RELAXED) == UPLIFT_LA_POLICY_SIMT)
+    return fail(UPLIFT_LA_ERR_UNSUPPORTED, "fused resize needs the tensor-core kernel (policy SIMT)");
+  if (I != 2) return fail(UPLIFT_LA_ERR_UNSUPPORTED, "fused resize: scale I=%d != 2", I);
+  int64_t gs[4] = {guide_strides[0], guide_strides[1], guide_strides[2], guide_strides[3]};
+  int64_t vs[4] = {value_strides[0], value_strides[1], value_strides[2], value_strides[3]};
+  int64_t os[4] = {out_strides[0], out_strides[1], out_strides[2], out_strides[3]};
+  canon_strides(gs, Cg, I * H, I * W, B);
+  canon_strides(vs, C, H, W, B);
+  canon_strides(os, C, Ho, Wo, B);
+  TcArgs a;
+  a.guide = guide; a.g_b = gs[0]; a.g_h = gs[2]; a.g_w = gs[3];
+  a.value = value; a.v_b = vs[0]; a.v_h = vs[2]; a.v_w = vs[3];
+  a.out = out; a.o_b = os[0]; a.o_h = os[2]; a.o_w = os[3];
+  a.weight = weight; a.bias = bias;
+  a.B = B; a.Cg = Cg; a.C = C; a.H = H; a.W = W; a.K = K; a.pn = pn;
+  a.conv_res = conv_res ? 1 : 0; a.hardmax = hardmax ? 1 : 0; a.dtype = dtype; a.offsets = offsets;
+  a.Ho = Ho; a.Wo = Wo;
+  const char* why = nullptr;
+  if (!tc_eligible(a, &why) || !tc_resize_eligible(a, &why))
+    return fail(UPLIFT_LA_ERR_UNSUPPORTED, "fused resize not applicable: %s", why);
+  const int rc = tc_launch(a, static_cast<cudaStream_t>(stream));
+  if (rc == UPLIFT_LA_OK) g_last_kernel = UPLIFT_LA_KERNEL_TENSOR_CORE_RESIZE;
+  return rc;
+}
+
 int uplift_la_pool(const void* logits, const int64_t logits_strides[4],
                    const void* value, const int64_t value_strides[4],
                    void* out, const int64_t out_strides[4],
@@ -343,6 +396,7 @@ const char* uplift_la_status_string(int status) {
     case UPLIFT_LA_ERR_OFFSETS: return "bad neighbour offsets";
     case UPLIFT_LA_ERR_CUDA: return "CUDA error";
     case UPLIFT_LA_ERR_NO_DEVICE: return "no usable sm_100 device";
+    case UPLIFT_LA_ERR_UNSUPPORTED: return "no fused kernel for this problem";
     default: return "unknown status";
   }
 }

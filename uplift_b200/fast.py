@@ -102,6 +102,13 @@ class OptimizedUPLiFT(nn.Module):
             else:
                 enc_feats = ex_feats
             x = _decoder(m.decoder, x, enc_feats)
+            # the last attender call also applies the final resize when
+            # nothing runs between the two (one launch, the attender output
+            # is never stored)
+            fuse = (outsize is not None and i == m.iters - 1 and m.refiner is None
+                    and isinstance(m.attender, AttenderWrapper))
+            if fuse:
+                return m.attender(x, x_in, size=tuple(outsize))
             if m.attender is not None:
                 x = m.attender(x, x_in)
             if m.refiner is not None:

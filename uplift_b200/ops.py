@@ -104,6 +104,57 @@ def local_attender_raw(guide: torch.Tensor, value: torch.Tensor, weight: torch.T
     return out
 
 
+def local_attender_resized_raw(guide: torch.Tensor, value: torch.Tensor, weight: torch.Tensor,
+                               bias: Optional[torch.Tensor], offsets: Sequence, pn: int, size: Sequence[int],
+                               conv_res: bool = True, hardmax: bool = False) -> torch.Tensor:
+    """The attender followed by F.interpolate(size, mode="bilinear",
+    align_corners=False): one launch of uplift_la_forward_resized when the
+    fused kernel applies (the attender output is never stored), else the
+    attender kernel and the glue resize kernel one after the other (same
+    values up to the fp32 contraction order of the resize)."""
+    dev = _check_cuda(guide, value, weight)
+    if guide.dtype != value.dtype:
+        raise ValueError(f"guide dtype {guide.dtype} != value dtype {value.dtype}")
+    if value.dtype not in _DTYPES:
+        raise ValueError(f"unsupported dtype {value.dtype} (float32, bfloat16, float16)")
+    B, C, H, W = value.shape
+    Bg, Cg, Ho_a, Wo_a = guide.shape
+    if Bg != B:
+        raise ValueError(f"batch mismatch: guide {Bg} vs value {B}")
+    I = _scale(Ho_a, Wo_a, H, W)
+    Ho, Wo = int(size[0]), int(size[1])
+    K = len(offsets)
+    w = weight.detach().reshape(K, -1)
+    if w.shape[1] != Cg:
+        raise ValueError(f"weight has {w.shape[1]} input channels, guide has {Cg}")
+    if w.dtype != torch.float32 or not w.is_contiguous():
+        w = w.to(torch.float32).contiguous()
+    b = None
+    if bias is not None:
+        b = bias.detach()
+        if b.dtype != torch.float32 or not b.is_contiguous():
+            b = b.to(torch.float32).contiguous()
+    g = _nhwc(guide)
+    v = _nhwc(value)
+    out = torch.empty((B, C, Ho, Wo), dtype=value.dtype, device=dev, memory_format=torch.channels_last)
+    lib = _native.load()
+    _native.host_status.raise_if_set()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        rc = lib.uplift_la_forward_resized(
+            g.data_ptr(), _native.strides(g), v.data_ptr(), _native.strides(v),
+            w.data_ptr(), None if b is None else b.data_ptr(),
+            out.data_ptr(), _native.strides(out),
+            B, Cg, C, H, W, I, K, _native.offsets_array(offsets), int(pn), int(bool(conv_res)),
+            _DTYPES[value.dtype], int(bool(hardmax)), Ho, Wo, stream)
+    if rc == _native.ERR_UNSUPPORTED:
+        from . import glue
+        y = local_attender_raw(guide, value, w, b, offsets, pn, conv_res, hardmax)
+        return glue.resize_bilinear_raw(y, (Ho, Wo))
+    _native.check(rc, "uplift_la_forward_resized")
+    return out
+
+
 def attender_pool_raw(logits: torch.Tensor, value: torch.Tensor, offsets: Sequence, pn: int,
                       hardmax: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Launch uplift_la_pool on pre-projected logits [B, K, I*H, I*W]."""
@@ -210,6 +261,19 @@ def _la_backward(ctx, grad):
 torch.library.register_autograd("uplift_b200::local_attender", _la_backward, setup_context=_la_setup_context)
 
 
+@torch.library.custom_op("uplift_b200::local_attender_resized", mutates_args=())
+def _local_attender_resized_op(guide: torch.Tensor, value: torch.Tensor, weight: torch.Tensor,
+                               bias: Optional[torch.Tensor], offsets: list[int], pn: int, size: list[int],
+                               conv_res: bool, hardmax: bool) -> torch.Tensor:
+    return local_attender_resized_raw(guide, value, weight, bias, _pairs(offsets), pn, size, conv_res, hardmax)
+
+
+@_local_attender_resized_op.register_fake
+def _(guide, value, weight, bias, offsets, pn, size, conv_res, hardmax):
+    B, C = value.shape[0], value.shape[1]
+    return value.new_empty((B, C, int(size[0]), int(size[1]))).contiguous(memory_format=torch.channels_last)
+
+
 @torch.library.custom_op("uplift_b200::attender_pool", mutates_args=())
 def _attender_pool_op(logits: torch.Tensor, value: torch.Tensor, offsets: list[int], pn: int,
                       hardmax: bool) -> torch.Tensor:
@@ -227,6 +291,14 @@ def local_attender(guide, value, weight, bias, offsets, pn, conv_res=True, hardm
     """Fused Local Attender (custom op entry; traceable by torch.compile)."""
     return torch.ops.uplift_b200.local_attender(guide, value, weight, bias, _offsets_flat(offsets),
                                                 int(pn), bool(conv_res), bool(hardmax))
+
+
+def local_attender_resized(guide, value, weight, bias, offsets, pn, size, conv_res=True, hardmax=False):
+    """Fused Local Attender + final bilinear resize to `size` (custom op
+    entry; inference only -- it has no autograd formula)."""
+    return torch.ops.uplift_b200.local_attender_resized(guide, value, weight, bias, _offsets_flat(offsets),
+                                                        int(pn), [int(size[0]), int(size[1])],
+                                                        bool(conv_res), bool(hardmax))
 
 
 def attender_pool(logits, value, offsets, pn, hardmax=False):
