@@ -79,3 +79,17 @@ def test_tf32_mode_scopes_the_switches():
         assert (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32) == (False, True)
     finally:
         torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = old
+
+
+def test_bf16_upsampler_fixture_inputs_regenerate():
+    """The inputs of the bf16 upsampler goldens come back from their seeds
+    bit for bit (the GPU test regenerates them instead of storing them)."""
+    import sys
+    sys.path.insert(0, str(GOLDEN))
+    from make_golden_bf16_upsampler import inputs, sha
+    gold = torch.load(GOLDEN / "upsampler_bf16_bands.pt", weights_only=False)
+    assert len(gold["cases"]) == 3
+    for case in gold["cases"]:
+        img, feats = inputs(case["img_px"], case["feat_px"], 384, case["seed"])
+        assert sha(img) == case["img_sha"] and sha(feats) == case["feats_sha"]
+        assert case["bands"].shape[0] == 3 and case["channel_sum"].shape == (384,)

@@ -22,13 +22,22 @@
 // offset is clamped to the image before being mapped to a window column
 // (clamped duplicates are merged in fp32 first).
 //
-// Roles (320 threads, one CTA per SM, persistent over tiles):
-//   warp 0      TMA producer: guide tile, value window in 64-channel chunks
-//   warp 1      TMEM owner + single-thread MMA issuer
-//   warps 2-5   logits -> (+bias, +residual) -> softmax -> A matrix
-//   warps 6-9   TMEM -> registers -> storage type -> smem -> TMA store
-// Every mbarrier wait is bounded (2 s); on expiry the CTA records an error
-// code in a device status word, drains its outstanding async work and exits.
+// Roles (608 threads = 19 warps, one CTA per SM, persistent over work
+// units -- tiles, or for grids with few tiles each tile's two accumulator
+// halves):
+//   warp 0      TMA producer of the value windows (64-channel chunks, one
+//               ring unit of <= 3 chunks per accumulator half)
+//   warp 18     TMA producer of the guide tiles
+//   warp 1      TMEM owner + single-thread MMA issuer (logits of unit n+1
+//               before the output MMAs of unit n)
+//   warps 2-9   two softmax warpgroups (even / odd units): logits -> (+bias,
+//               +residual) -> softmax -> A matrix
+//   warps 10-17 two epilogue warpgroups, one per 192-column accumulator
+//               half: TMEM -> storage type -> smem -> TMA store (or, with
+//               the fused final resize, -> bilinear resample -> TMA store)
+// Every mbarrier wait is bounded (2 s); on expiry the CTA records the role
+// in a device status word (and a host-visible word when one is registered),
+// drains its outstanding async work and exits.
 //
 // Reference semantics: LocalAttender.forward, uplift/uplift.py:801-847.
 
@@ -74,6 +83,7 @@ constexpr int kTmemCols = 512;
 constexpr int kThreads = 608;                // 19 warps
 constexpr int kGuideWarp = 18;               // guide-tile producer
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // default limit of every mbarrier wait
+constexpr int kSplitTilesPerSm = 8;          // split tiles into halves below this many tiles per SM
 
 constexpr int kVBytes = kWin * 128;          // 12 KB: 96 window px x 64 ch
 constexpr int kGBytes = kM * 128;            // 16 KB: 128 px x 64 guide ch
@@ -113,6 +123,8 @@ struct Params {
   int8_t dy[kLogN];
   int8_t dx[kLogN];
   int H, W, nchunks, tiles_x, tiles_y, num_tiles;
+  int split;            // 1: a work unit is one accumulator half of a tile
+  int num_units;        // num_tiles, or 2 * num_tiles with the split
   int res_k;            // residual channels (min(K, Cg) when conv_res, else 0)
   int hardmax;
   int margin;           // max |offset| (cells this close to a border may clamp)
@@ -165,6 +177,32 @@ __device__ __forceinline__ TileXY tile_of(const Params& p, int t) {
   r.cy0 = ty * kCellsY;
   r.cx0 = (rem - ty * p.tiles_x) * kCellsX;
   return r;
+}
+
+// A CTA's work unit n: a tile, or with the split one accumulator half of a
+// tile (for grids with few tiles, so that every CTA still pipelines several
+// units).  The two halves of a tile are consecutive global units, which run
+// at the same time on neighbouring CTAs (the second read of the guide tile
+// hits L2); along a CTA's units the half alternates, so that both epilogue
+// warpgroups work.
+struct Unit {
+  TileXY t;
+  int hmask;  // accumulator halves of this unit: 3 = both, else 1 << half
+};
+__device__ __forceinline__ Unit unit_of(const Params& p, int n) {
+  const int g = blockIdx.x + n * gridDim.x;
+  Unit u;
+  if (!p.split) {
+    u.t = tile_of(p, g);
+    u.hmask = 3;
+    return u;
+  }
+  u.t = tile_of(p, g >> 1);
+  // an even grid keeps g's parity fixed per CTA: alternate it with n (the
+  // halves of units 2t and 2t + 1 still differ, as both have the same n)
+  const int half = (gridDim.x & 1) ? (g & 1) : ((g ^ n) & 1);
+  u.hmask = 1 << half;
+  return u;
 }
 
 template <typename T, int K, bool RS>
@@ -241,8 +279,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  int local_tiles = 0;
-  for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) ++local_tiles;
+  int local_units = 0;
+  for (int t = blockIdx.x; t < p.num_units; t += gridDim.x) ++local_units;
   const WaitLimit tmo{p.timeout_ns, p.host_status};
   const int half_chunks = (p.nchunks + 1) / 2;
 
@@ -256,8 +294,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       bool ok = true;
       if (warp == kGuideWarp) {
         prefetch_map(&p.gmap);
-        for (int n = 0; n < local_tiles && ok; ++n) {
-          const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+        for (int n = 0; n < local_units && ok; ++n) {
+          const TileXY tl = unit_of(p, n).t;
           const int s = n & 1;
           ok = mbar_wait(&g_empty[s], ((n >> 1) & 1) ^ 1, abort_flag, 1, tmo);
           if (!ok) break;
@@ -269,13 +307,14 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
         prefetch_map(&p.vmap);
         prefetch_map(&p.omap);
         uint32_t vc = 0;
-        for (int n = 0; n < local_tiles && ok; ++n) {
-          const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+        for (int n = 0; n < local_units && ok; ++n) {
+          const Unit u = unit_of(p, n);
+          const TileXY tl = u.t;
           // value window, one ring unit per accumulator half (<= 3 chunks of
           // 64 channels, contiguous so that one MMA spans them)
           for (int h = 0; h < 2 && ok; ++h) {
             const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
-            if (j0 >= j1) continue;
+            if (j0 >= j1 || !((u.hmask >> h) & 1)) continue;
             const int slot = vc % kNU;
             ok = mbar_wait(&v_empty[slot], ((vc / kNU) & 1) ^ 1, abort_flag, 1, tmo);
             if (!ok) break;
@@ -314,9 +353,11 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
         tc_commit(&g_empty[s]);
         return true;
       };
-      if (local_tiles > 0) ok = logits(0);
-      for (int n = 0; n < local_tiles && ok; ++n) {
-        if (n + 1 < local_tiles) {
+      uint32_t hcnt[2] = {0, 0};  // units so far per accumulator half
+      if (local_units > 0) ok = logits(0);
+      for (int n = 0; n < local_units && ok; ++n) {
+        const int hmask = unit_of(p, n).hmask;
+        if (n + 1 < local_units) {
           ok = logits(n + 1);
           if (!ok) break;
         }
@@ -330,8 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
         // MMAs of the other
         for (int h = 0; h < 2 && ok; ++h) {
           const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
-          if (j0 >= j1) continue;
-          ok = mbar_wait(&out_empty[h], (n & 1) ^ 1, abort_flag, 2, tmo);
+          if (j0 >= j1 || !((hmask >> h) & 1)) continue;
+          ok = mbar_wait(&out_empty[h], (hcnt[h] & 1) ^ 1, abort_flag, 2, tmo);
           if (!ok) break;
           tc_fence_after();
           const int slot = vc % kNU;
@@ -348,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
           tc_commit(&v_empty[slot]);
           if (!ok) break;
           tc_commit(&out_full[h]);
+          ++hcnt[h];
         }
         if (!ok) break;
         tc_commit(&a2_empty[s]);
@@ -367,8 +409,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     const int py = i >> 4, px = i & 15;
     const int cr = py >> 1, cc = px >> 1;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-    for (int n = wg; n < local_tiles; n += 2) {
-      const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+    for (int n = wg; n < local_units; n += 2) {
+      const TileXY tl = unit_of(p, n).t;
       const int s = n & 1;
       const uint32_t ph = (n >> 1) & 1;
       if (!mbar_wait(&log_full[s], ph, abort_flag, 3, tmo)) break;
@@ -470,9 +512,13 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     uint8_t* bufs = sStage + (warp - 10) * 2 * kWarpStage;  // two staging buffers per warp
     uint32_t jw = 0;
     const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
-    for (int n = 0; n < local_tiles && j0 < j1; ++n) {
-      const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
-      if (!mbar_wait(&out_full[h], n & 1, abort_flag, 4, tmo)) break;
+    uint32_t cnt = 0;  // units of this half so far
+    for (int n = 0; n < local_units && j0 < j1; ++n) {
+      const Unit u = unit_of(p, n);
+      if (!((u.hmask >> h) & 1)) continue;
+      const TileXY tl = u.t;
+      if (!mbar_wait(&out_full[h], cnt & 1, abort_flag, 4, tmo)) break;
+      ++cnt;
       tc_fence_after();
       for (int j = j0; j < j1; ++j) {
         uint32_t r[64];
@@ -532,9 +578,13 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     const int oc = t >> 3;  // output column of the tile (< 14) this thread resamples
     const int cg = t & 7;   // its 16-byte channel group
     const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
-    for (int n = 0; n < local_tiles && j0 < j1; ++n) {
-      const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
-      if (leader) *go = mbar_wait(&out_full[h], n & 1, abort_flag, 4, tmo) ? 1 : 0;
+    uint32_t cnt = 0;  // units of this half so far
+    for (int n = 0; n < local_units && j0 < j1; ++n) {
+      const Unit u = unit_of(p, n);
+      if (!((u.hmask >> h) & 1)) continue;  // the same decision in all 128 threads
+      const TileXY tl = u.t;
+      if (leader) *go = mbar_wait(&out_full[h], cnt & 1, abort_flag, 4, tmo) ? 1 : 0;
+      ++cnt;
       named_bar(bar_t, 128);
       if (*go == 0) break;
       tc_fence_after();
@@ -842,7 +892,18 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (dev >= 0 && dev < 64) sm_count[dev].store(sms, std::memory_order_relaxed);
   }
-  const int grid = (int)std::min<int64_t>(nt, std::max(sms, 1));
+  // Grids with few tiles per SM (the first levels of the upsampler) split
+  // every tile into its two accumulator halves, so each CTA pipelines
+  // several units instead of running one or two tiles start to finish.
+  static const int split_below = [] {
+    const char* e = getenv("ULA_TC_SPLIT_TILES_PER_SM");
+    return e != nullptr ? atoi(e) : kSplitTilesPerSm;
+  }();
+  p.split = (p.nchunks >= 2 && nt < (int64_t)split_below * std::max(sms, 1)) ? 1 : 0;
+  const int64_t units = nt * (p.split ? 2 : 1);
+  if (units >= (1ll << 31)) return fail(UPLIFT_LA_ERR_SHAPE, "too many tiles");
+  p.num_units = (int)units;
+  const int grid = (int)std::min<int64_t>(units, std::max(sms, 1));
   if (rs)
     return a.dtype == UPLIFT_LA_BF16 ? launch_k<__nv_bfloat16, true>(p, a.K, dev, grid, stream)
                                      : launch_k<__half, true>(p, a.K, dev, grid, stream);
