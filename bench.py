@@ -314,6 +314,8 @@ def run_ours(args, world, rank, local):
 
     # ---- fp32 attender configurations (standalone K=9 call, SD1.5-VAE levels)
     fp32 = None if args.no_fp32 else run_fp32_configs(dev, stream, peak)
+    glue_rl = None if args.no_upsampler else run_glue_rooflines(dev, stream, peak)
+    fused_rs = None if args.no_upsampler else run_fused_resize(dev, stream, peak)
 
     # ---- attender backward (training) on the same four levels
     bwd = None if args.no_backward else run_backward(dev, stream, peak, B_PER_GPU)
@@ -353,6 +355,10 @@ def run_ours(args, world, rank, local):
         result["upsampler_other_configs"] = models
     if fp32 is not None:
         result["fp32_configs"] = fp32
+    if glue_rl is not None:
+        result["glue_rooflines"] = glue_rl
+    if fused_rs is not None:
+        result["fused_resize"] = fused_rs
     if bwd is not None:
         result["backward"] = bwd
     if cpu is not None:
@@ -375,6 +381,7 @@ def summary(r):
             "e2e_Mpix_s": get("e2e", "value"), "e2e_copy_frac": get("e2e", "copy_roofline", "e2e_frac"),
             "triton_ref_Mpix_s": get("triton_reference", "Mpix_s"),
             "cfg5_img_s": get("upsampler", "img_per_s"),
+            "fused_resize_speedup": get("fused_resize", "speedup"),
             "cfg5_img_s_gather": get("upsampler", "gather", "img_per_s"),
             "cfg3_img_s": get("upsampler_other_configs", "dinov3_splus16_512_b32_bf16", "img_per_s"),
             "cfg4_img_s": get("upsampler_other_configs", "sd15_vae_512_b16_fp32", "img_per_s"),
@@ -436,6 +443,102 @@ def run_triton_reference(dev, stream, la, value0, guides, ours_out, ours_ms_step
             "normwise_diff_vs_ours": round(err, 5),
             "path": "reference _TritonAttenderWrapper + TritonLocalAttender (baseline/_ref, unmodified), "
                     "eager, bf16, same inputs and weights"}
+
+
+def run_fused_resize(dev, stream, peak, reps=5):
+    """The last attender call of the 1022 px DINOv2 upsampler (B=8, value
+    384 x 584^2, guide 64 x 1168^2, bf16) with the final resize to 1022^2:
+    the two launches (attender writes 1168^2, the resize kernel reads it back)
+    against uplift_la_forward_resized (one launch, the 1168^2 tensor is never
+    stored).  CUDA events, median of `reps`.  Algorithmic bytes of the fused
+    call: guide + value once + the 1022^2 output."""
+    from uplift_b200 import glue, ops
+    from uplift_b200.attender import neighbourhood
+    K, B, Cv, side = K_NBR, 8, C, 584
+    offsets, pn = neighbourhood(K)
+    g = torch.Generator(device=dev).manual_seed(5)
+    cl = torch.channels_last
+    guide = torch.randn(B, CG, 2 * side, 2 * side, generator=g, device=dev).to(torch.bfloat16).contiguous(memory_format=cl)
+    value = torch.randn(B, Cv, side, side, generator=g, device=dev).to(torch.bfloat16).contiguous(memory_format=cl)
+    w = torch.randn(K, CG, generator=g, device=dev) * 0.1
+    b = torch.randn(K, generator=g, device=dev) * 0.1
+
+    def timed(fn):
+        fn()
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    with torch.cuda.stream(stream):
+        two = timed(lambda: glue.resize_bilinear(ops.local_attender_raw(guide, value, w, b, offsets, pn), (1022, 1022)))
+        one = timed(lambda: ops.local_attender_resized_raw(guide, value, w, b, offsets, pn, (1022, 1022)))
+    del guide, value
+    torch.cuda.empty_cache()
+    algo = B * (2 * side) ** 2 * (CG * ELEM + Cv * ELEM / 4) + B * 1022 * 1022 * Cv * ELEM
+    return {"two_launches_ms": round(two, 4), "fused_ms": round(one, 4), "speedup": round(two / one, 3),
+            "fused_GB_s": round(algo / one / 1e6, 1), "fused_frac_of_peak": round(algo / one / 1e6 / peak, 4),
+            "algo_bytes": int(algo),
+            "shape": "B=8, value 384x584^2 -> attender 1168^2 -> bilinear 1022^2, bf16, K=17"}
+
+
+def run_glue_rooflines(dev, stream, peak, reps=5):
+    """Achieved HBM bandwidth of the fast-mode glue kernels
+    (include/uplift_glue.h) at the shapes of the 1022 px DINOv2 upsampler's
+    last level (one micro-batch of 8 images, bf16, channels_last): each
+    call timed alone with CUDA events (median of `reps` after a warm call;
+    every operand is larger than L2).  Algorithmic bytes: every input
+    element read once and every output element written once (in-place
+    operands count twice)."""
+    from uplift_b200 import glue
+    cl = torch.channels_last
+    bf = torch.bfloat16
+    B, S = 8, 1168
+
+    def t(c, h, w=None):
+        return torch.randn(B, c, h, w or h, device=dev, dtype=bf).contiguous(memory_format=cl)
+
+    def timed(fn):
+        fn()
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    out = {}
+    with torch.cuda.stream(stream):
+        y, r = t(64, S), t(64, S)
+        bias = torch.randn(64, device=dev, dtype=bf)
+        ms = timed(lambda: glue.bias_act_(y, bias, True, r))
+        out["bias_act_relu_res_64ch_1168"] = (ms, 3 * y.numel() * 2)
+        x = t(64, S // 2)
+        ms = timed(lambda: glue.upsample_add_(y, x, align_corners=True))
+        out["upsample_add_64ch_584to1168"] = (ms, (2 * y.numel() + x.numel()) * 2)
+        del x, r
+        buf = torch.empty(B, 192, S // 2, S // 2, device=dev, dtype=bf, memory_format=cl)
+        skip = t(128, S)
+        ms = timed(lambda: glue.nearest_into_(buf[:, 64:], skip))
+        out["nearest_into_128ch_1168to584"] = (ms, 2 * B * 128 * (S // 2) ** 2 * 2)
+        del buf, skip, y
+        a = t(384, S)
+        ms = timed(lambda: glue.resize_bilinear(a, (1022, 1022)))
+        out["bilinear_384ch_1168to1022"] = (ms, (a.numel() + B * 384 * 1022 * 1022) * 2)
+        del a
+    torch.cuda.empty_cache()
+    return {k: {"ms": round(ms, 4), "GB_s": round(b / ms / 1e6, 1), "frac_of_peak": round(b / ms / 1e6 / peak, 4)}
+            for k, (ms, b) in out.items()} | {
+        "note": "B=8, bf16, channels_last; single calls, median of 5; algorithmic bytes; "
+                "frac against the measured HBM copy peak"}
 
 
 def run_fp32_configs(dev, stream, peak, reps=20):

@@ -110,6 +110,44 @@ int uplift_la_forward_resized(const void* guide, const int64_t guide_strides[4],
                               int dtype, int hardmax, int Ho, int Wo, void* stream);
 
 /*
+ * The guide produced inside the attender launch.  In the DINOv2 / DINOv3
+ * decoders the guide is the output of the last block, a residual DoubleConv
+ * whose final layer is a 1x1 convolution with bias
+ * (uplift/uplift.py:152-217): guide = w_guide . act + b_guide + res, where
+ * `act` is that block's activation before the 1x1 convolution and `res` the
+ * first Cg channels of the block's input (residual_auto's truncation,
+ * uplift/uplift.py:26-39).  This entry point computes
+ * uplift_la_forward(guide, ...) from act and res directly -- the guide is
+ * never stored -- by folding the 1x1 convolution and both residuals into
+ * the projection: logits = (A . w_guide) act + A res + bias + A b_guide, A =
+ * weight plus the identity on the first K channels when conv_res.  The
+ * folded [K, 2 Cg] projection is computed in fp32 in the kernel prologue and
+ * rounded once to the storage type (the unfused path rounds the guide
+ * instead; both are within the storage type's precision).
+ *
+ *   act, res   [B, Cg, I*H, I*W] (strides; res may be a channel slice)
+ *   w_guide    [Cg, Cg] fp32 (out, in): the block's 1x1 conv weight
+ *   b_guide    [Cg] fp32 or NULL: its bias
+ *   Ho, Wo     0, 0: out is [B, C, I*H, I*W]; else the output also gets the
+ *              final resize of uplift_la_forward_resized and is [B, C, Ho, Wo]
+ *
+ * Applies to the tensor-core kernel's problems (bf16 / fp16, I = 2, Cg = 64,
+ * C a multiple of 64 up to 384; with a resize, its conditions too);
+ * otherwise returns UPLIFT_LA_ERR_UNSUPPORTED and launches nothing.  No
+ * single reference counterpart (it fuses the decoder's last 1x1 conv and
+ * residual, uplift/uplift.py:172 and :208-215, into the attender).
+ */
+int uplift_la_forward_fused_guide(const void* act, const int64_t act_strides[4],
+                                  const void* res, const int64_t res_strides[4],
+                                  const float* w_guide, const float* b_guide,
+                                  const void* value, const int64_t value_strides[4],
+                                  const float* weight, const float* bias,
+                                  void* out, const int64_t out_strides[4],
+                                  int B, int Cg, int C, int H, int W, int I, int K,
+                                  const int8_t* offsets, int pn, int conv_res,
+                                  int dtype, int hardmax, int Ho, int Wo, void* stream);
+
+/*
  * Softmax-pool from pre-projected logits: the same kernel with the
  * projection replaced by a read of `logits` [B, K, I*H, I*W] (any strides,
  * same storage type as value).  Replaces the Triton fused kernels'
@@ -205,6 +243,8 @@ int uplift_la_set_kernel_policy(int policy);
 #define UPLIFT_LA_KERNEL_SIMT_STAGED 3  /* CUDA-core kernel, guide staged in shared memory */
 #define UPLIFT_LA_KERNEL_TENSOR_CORE_WIDE 4  /* fp32, wide guide: split-bf16 tensor-core projection */
 #define UPLIFT_LA_KERNEL_TENSOR_CORE_RESIZE 5  /* tensor-core kernel with the fused final resize */
+#define UPLIFT_LA_KERNEL_TENSOR_CORE_GUIDE 6   /* tensor-core kernel, guide produced inside */
+#define UPLIFT_LA_KERNEL_TENSOR_CORE_GUIDE_RESIZE 7  /* both fusions */
 int uplift_la_last_kernel(void);
 
 /* Device status word of the tensor-core kernels: 0 when every launch so far

@@ -23,6 +23,7 @@ NOALLOC_MAX_PROBS = 8 * 1024 * 1024  # floats, UPLIFT_LA_NOALLOC_MAX_PROBS
 EXPORTED = (
     "uplift_la_forward",
     "uplift_la_forward_resized",
+    "uplift_la_forward_fused_guide",
     "uplift_la_pool",
     "uplift_la_last_error",
     "uplift_la_status_string",
@@ -44,6 +45,7 @@ EXPORTED = (
 POLICY_AUTO, POLICY_SIMT, POLICY_TENSOR_CORE = 0, 1, 2
 KERNEL_SIMT, KERNEL_TENSOR_CORE, KERNEL_SIMT_STAGED, KERNEL_TENSOR_CORE_WIDE = 1, 2, 3, 4
 KERNEL_TENSOR_CORE_RESIZE = 5
+KERNEL_TENSOR_CORE_GUIDE, KERNEL_TENSOR_CORE_GUIDE_RESIZE = 6, 7
 KERNELS_CUDA_CORE = (KERNEL_SIMT, KERNEL_SIMT_STAGED)
 
 _lib = None
@@ -83,6 +85,9 @@ def load(build_if_missing: bool = False):
         lib.uplift_la_forward_resized.restype = i
         lib.uplift_la_forward_resized.argtypes = [vp, i64p, vp, i64p, fp, fp, vp, i64p,
                                                   i, i, i, i, i, i, i, i8p, i, i, i, i, i, i, vp]
+        lib.uplift_la_forward_fused_guide.restype = i
+        lib.uplift_la_forward_fused_guide.argtypes = [vp, i64p, vp, i64p, fp, fp, vp, i64p, fp, fp, vp, i64p,
+                                                      i, i, i, i, i, i, i, i8p, i, i, i, i, i, i, vp]
         lib.uplift_la_pool.restype = i
         lib.uplift_la_pool.argtypes = [vp, i64p, vp, i64p, vp, i64p,
                                        i, i, i, i, i, i, i8p, i, i, i, vp]

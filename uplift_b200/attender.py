@@ -165,3 +165,14 @@ class AttenderWrapper(nn.Module):
                                               conv_res=self.conv_res, hardmax=hardmax)
         return ops.local_attender(guide, value, w, b, self.offsets, self.pn,
                                   conv_res=self.conv_res, hardmax=hardmax)
+
+    def forward_fused_guide(self, act, res, guide_conv, value, hardmax=False, size=None):
+        """forward(guide, value) for guide = guide_conv(act) + res[:, :Cg]
+        -- the decoder's last residual block with its final 1x1 convolution
+        (uplift/uplift.py:152-217) -- without storing the guide: the 1x1
+        convolution and both residuals are folded into the attender's
+        projection in the same launch (`size`: also the final resize)."""
+        w, b = _fp32_projection(self, self.conv1, self.num_connected)
+        return ops.local_attender_fused_guide(act, res, guide_conv.weight, guide_conv.bias, value, w, b,
+                                              self.offsets, self.pn, conv_res=self.conv_res, hardmax=hardmax,
+                                              size=size)

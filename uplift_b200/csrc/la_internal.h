@@ -22,6 +22,12 @@ struct TcArgs {
   // fused final resize: out is [B, Ho, Wo, C], the bilinear
   // (align_corners=False) resize of the attender output; 0 = no resize
   int Ho = 0, Wo = 0;
+  // fused guide: `guide` is the guide block's activation h and guide2 its
+  // residual input u (same sizes, Cg channels each); guide = w_guide . h +
+  // b_guide + u is folded into the projection.  guide2 = null: plain guide.
+  const void* guide2 = nullptr; int64_t g2_b = 0, g2_h = 0, g2_w = 0;
+  const float* w_guide = nullptr;  // [Cg][Cg] fp32 (out, in)
+  const float* b_guide = nullptr;  // [Cg] fp32 or null
 };
 
 // True when the tensor-core kernel supports the problem (sizes, alignment).
@@ -58,9 +64,10 @@ unsigned int* host_status_word();
 // Record an error message for uplift_la_last_error().
 int fail(int code, const char* fmt, ...);
 
-// NHWC 4-D TMA map with the 128-byte swizzle (dims {C, W, H, B}, strides in
-// elements of `es` bytes).
+// NHWC 4-D TMA map (dims {C, W, H, B}, strides in elements of `es` bytes),
+// with the 128-byte swizzle unless another is asked for.
 int tc_make_map(CUtensorMap* map, CUtensorMapDataType dt, int es, const void* base, int C, int W, int H, int B,
-                int64_t s_w, int64_t s_h, int64_t s_b, int box_c, int box_w, int box_h);
+                int64_t s_w, int64_t s_h, int64_t s_b, int box_c, int box_w, int box_h,
+                CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 }  // namespace ula

@@ -22,9 +22,7 @@
 // offset is clamped to the image before being mapped to a window column
 // (clamped duplicates are merged in fp32 first).
 //
-// Roles (608 threads = 19 warps, one CTA per SM, persistent over work
-// units -- tiles, or for grids with few tiles each tile's two accumulator
-// halves):
+// Roles (608 threads = 19 warps, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer of the value windows (64-channel chunks, one
 //               ring unit of <= 3 chunks per accumulator half)
 //   warp 18     TMA producer of the guide tiles
@@ -83,12 +81,11 @@ constexpr int kTmemCols = 512;
 constexpr int kThreads = 608;                // 19 warps
 constexpr int kGuideWarp = 18;               // guide-tile producer
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // default limit of every mbarrier wait
-constexpr int kSplitTilesPerSm = 8;          // split tiles into halves below this many tiles per SM
 
 constexpr int kVBytes = kWin * 128;          // 12 KB: 96 window px x 64 ch
 constexpr int kGBytes = kM * 128;            // 16 KB: 128 px x 64 guide ch
 constexpr int kStageBytes = kM * 128;        // 16 KB: 128 px x 64 out ch
-constexpr int kWBytes = kLogN * 128;         // 4 KB: 32 logits x 64 ch
+constexpr int kWBytes = kLogN * 128;         // 4 KB: 32 logits x 64 ch (one guide source)
 constexpr int kA2Bytes = kM * kWin * 2;      // 24 KB
 constexpr int kA2Sbo = (kWin / 8) * 128;     // 1536 B between 8-row groups of A
 
@@ -97,20 +94,26 @@ constexpr int kUnitBytes = kUnitChunks * kVBytes;  // 36 KB
 constexpr int kOffG = kOffV + kNU * kUnitBytes;
 constexpr int kOffStage = kOffG + 2 * kGBytes;
 constexpr int kOffW = kOffStage + 4 * kStageBytes;  // 8 epilogue warps x 2 x 4 KB
-constexpr int kOffA2 = kOffW + kWBytes;
+constexpr int kOffA2 = kOffW + 2 * kWBytes;  // two sources with the fused guide
 constexpr int kOffBar = kOffA2 + 2 * kA2Bytes;
 constexpr int kNumBars = 2 + 2 + kNU + kNU + 2 + 2 + 2 + 2 + 2 + 2 + 1;
 constexpr int kWarpStage = 32 * 128;         // 4 KB: one epilogue warp's 32 px x 64 ch
 constexpr int kOffMisc = kOffBar + kNumBars * 8;   // tmem slot, abort flag
 // Fused final resize (RS kernels): each epilogue warpgroup uses its half of
-// the staging region for one 8 x 16-pixel, 64-channel slice of the tile in
-// storage precision (T) and the 7 x 14 resized pixels made from it (O,
-// laid out as the TMA store box {64, 14, 7} with the 128-byte swizzle).
+// the staging region for two buffers T of one 8 x 16-pixel, 32-channel
+// slice of the tile in storage precision and two buffers O of the 7 x 14
+// resized pixels made from it (laid out as the TMA store box {32, 14, 7}
+// with the 64-byte swizzle: 16-byte chunk c of 64-byte row r sits at
+// chunk c ^ ((r >> 1) & 3); T uses the same layout).
 constexpr int kRsHalfBytes = 2 * kStageBytes;           // 32 KB per warpgroup
-constexpr int kRsTileBytes = kM * 128;                  // T: 16 KB
+constexpr int kRsChunk = 32;                            // channels per resize step
+constexpr int kRsTBytes = kM * 64;                      // T: 8 KB
 constexpr int kRsOutY = 7, kRsOutX = 14;                // resized pixels per tile
-constexpr int kRsOutBytes = kRsOutY * kRsOutX * 128;    // O: 12.25 KB (1024-aligned start)
-static_assert(kRsTileBytes + kRsOutBytes + 16 <= kRsHalfBytes, "resize staging exceeds the half region");
+constexpr int kRsOBytes = kRsOutY * kRsOutX * 64;       // O: 6272 B
+constexpr int kRsOSlot = 7 * 1024;                      // O slots 1024-aligned (swizzle atom)
+constexpr int kRsOffO = 2 * kRsTBytes;
+constexpr int kRsOffGo = kRsOffO + 2 * kRsOSlot;
+static_assert(kRsOBytes <= kRsOSlot && kRsOffGo + 16 <= kRsHalfBytes, "resize staging exceeds the half region");
 constexpr int kOffBias = kOffMisc + 16;
 constexpr int kSmemBytes = kOffBias + kLogN * 4 + 1024;  // + base alignment slack
 
@@ -123,9 +126,16 @@ struct Params {
   int8_t dy[kLogN];
   int8_t dx[kLogN];
   int H, W, nchunks, tiles_x, tiles_y, num_tiles;
-  int split;            // 1: a work unit is one accumulator half of a tile
-  int num_units;        // num_tiles, or 2 * num_tiles with the split
   int res_k;            // residual channels (min(K, Cg) when conv_res, else 0)
+  // fused guide (GF kernels): the guide is never stored.  gmap reads the
+  // guide block's activation h and gmap2 its residual input u (64 channels
+  // each); guide = w_guide . h + b_guide + u, and the prologue folds it into
+  // the projection: logits = [A . w_guide | A] . [h | u] + bias + A . b_guide
+  // with A = weight (+ the identity on the first K channels when conv_res).
+  CUtensorMap gmap2;
+  const float* w_guide;  // [64][64] fp32 (out, in)
+  const float* b_guide;  // [64] fp32 or null
+  int conv_res;
   int hardmax;
   int margin;           // max |offset| (cells this close to a border may clamp)
   uint64_t timeout_ns;  // limit of every mbarrier wait
@@ -179,34 +189,12 @@ __device__ __forceinline__ TileXY tile_of(const Params& p, int t) {
   return r;
 }
 
-// A CTA's work unit n: a tile, or with the split one accumulator half of a
-// tile (for grids with few tiles, so that every CTA still pipelines several
-// units).  The two halves of a tile are consecutive global units, which run
-// at the same time on neighbouring CTAs (the second read of the guide tile
-// hits L2); along a CTA's units the half alternates, so that both epilogue
-// warpgroups work.
-struct Unit {
-  TileXY t;
-  int hmask;  // accumulator halves of this unit: 3 = both, else 1 << half
-};
-__device__ __forceinline__ Unit unit_of(const Params& p, int n) {
-  const int g = blockIdx.x + n * gridDim.x;
-  Unit u;
-  if (!p.split) {
-    u.t = tile_of(p, g);
-    u.hmask = 3;
-    return u;
-  }
-  u.t = tile_of(p, g >> 1);
-  // an even grid keeps g's parity fixed per CTA: alternate it with n (the
-  // halves of units 2t and 2t + 1 still differ, as both have the same n)
-  const int half = (gridDim.x & 1) ? (g & 1) : ((g ^ n) & 1);
-  u.hmask = 1 << half;
-  return u;
-}
-
-template <typename T, int K, bool RS>
+template <typename T, int K, bool RS, bool GF>
 __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constant__ Params p) {
+  // guide tile slots: two single-source tiles, or one slot holding both
+  // sources of the fused guide (the softmax never reads it then, so the slot
+  // frees as soon as the logits MMA has completed)
+  constexpr int kGSlots = GF ? 1 : 2;
   using S = Store<T>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -238,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&g_full[i], 1);
-      mbar_init(&g_empty[i], 1 + 4);  // logits MMA done + 4 softmax warps read the residual
+      mbar_init(&g_empty[i], GF ? 1 : 1 + 4);  // logits MMA done (+ 4 softmax warps read the residual)
       mbar_init(&log_full[i], 1);
       mbar_init(&log_empty[i], 4);    // 4 softmax warps
       mbar_init(&a2_full[i], 4);      // 4 softmax warps
@@ -267,20 +255,51 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
   asm volatile("griddepcontrol.launch_dependents;");
   // Projection weights in the storage type, K-major with the 128-byte swizzle
   // (row n = logit n, 64 guide channels per 128-byte row).
-  for (int idx = tid; idx < kLogN * 64; idx += kThreads) {
-    const int n = idx >> 6, c = idx & 63;
-    const float w = (n < K) ? p.weight[n * 64 + c] : 0.f;
-    *reinterpret_cast<uint16_t*>(sW + n * 128 + ((((c >> 3) ^ (n & 7)) << 4)) + (c & 7) * 2) = S::bits(w);
+  if constexpr (!GF) {
+    for (int idx = tid; idx < kLogN * 64; idx += kThreads) {
+      const int n = idx >> 6, c = idx & 63;
+      const float w = (n < K) ? p.weight[n * 64 + c] : 0.f;
+      *reinterpret_cast<uint16_t*>(sW + n * 128 + ((((c >> 3) ^ (n & 7)) << 4)) + (c & 7) * 2) = S::bits(w);
+    }
+    for (int k = tid; k < kLogN; k += kThreads) sBias[k] = (p.bias != nullptr && k < K) ? p.bias[k] : 0.f;
+  } else {
+    // A = weight (+ identity on the first K channels with conv_res): source 0
+    // (h) gets A . w_guide, source 1 (u) gets A, the bias gains A . b_guide;
+    // computed in fp32, rounded once to the storage type
+    auto a_of = [&](int n, int j) {
+      return p.weight[n * 64 + j] + ((p.conv_res && j == n) ? 1.f : 0.f);
+    };
+    for (int idx = tid; idx < 2 * kLogN * 64; idx += kThreads) {
+      const int src = idx / (kLogN * 64), n = (idx >> 6) % kLogN, c = idx & 63;
+      float w = 0.f;
+      if (n < K) {
+        if (src == 1) {
+          w = a_of(n, c);
+        } else {
+          for (int j = 0; j < 64; ++j) w = fmaf(a_of(n, j), p.w_guide[j * 64 + c], w);
+        }
+      }
+      *reinterpret_cast<uint16_t*>(sW + src * kWBytes + n * 128 + ((((c >> 3) ^ (n & 7)) << 4)) + (c & 7) * 2) =
+          S::bits(w);
+    }
+    for (int k = tid; k < kLogN; k += kThreads) {
+      float bk = 0.f;
+      if (k < K) {
+        bk = p.bias != nullptr ? p.bias[k] : 0.f;
+        if (p.b_guide != nullptr)
+          for (int j = 0; j < 64; ++j) bk = fmaf(a_of(k, j), p.b_guide[j], bk);
+      }
+      sBias[k] = bk;
+    }
   }
-  for (int k = tid; k < kLogN; k += kThreads) sBias[k] = (p.bias != nullptr && k < K) ? p.bias[k] : 0.f;
   fence_proxy_async();  // sW is read by the tensor core (async proxy)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  int local_units = 0;
-  for (int t = blockIdx.x; t < p.num_units; t += gridDim.x) ++local_units;
+  int local_tiles = 0;
+  for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) ++local_tiles;
   const WaitLimit tmo{p.timeout_ns, p.host_status};
   const int half_chunks = (p.nchunks + 1) / 2;
 
@@ -294,27 +313,32 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       bool ok = true;
       if (warp == kGuideWarp) {
         prefetch_map(&p.gmap);
-        for (int n = 0; n < local_units && ok; ++n) {
-          const TileXY tl = unit_of(p, n).t;
-          const int s = n & 1;
-          ok = mbar_wait(&g_empty[s], ((n >> 1) & 1) ^ 1, abort_flag, 1, tmo);
+        for (int n = 0; n < local_tiles && ok; ++n) {
+          const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+          const int s = n % kGSlots;
+          ok = mbar_wait(&g_empty[s], ((n / kGSlots) & 1) ^ 1, abort_flag, 1, tmo);
           if (!ok) break;
           if (p.test_fault == 1) continue;  // the guide never arrives: consumers time out
-          mbar_expect_tx(&g_full[s], kGBytes);
-          tma_load(sG + s * kGBytes, &p.gmap, &g_full[s], 0, 2 * tl.cx0, 2 * tl.cy0, tl.b);
+          if constexpr (GF) {  // both sources into the one slot
+            mbar_expect_tx(&g_full[0], 2 * kGBytes);
+            tma_load(sG, &p.gmap, &g_full[0], 0, 2 * tl.cx0, 2 * tl.cy0, tl.b);
+            tma_load(sG + kGBytes, &p.gmap2, &g_full[0], 0, 2 * tl.cx0, 2 * tl.cy0, tl.b);
+          } else {
+            mbar_expect_tx(&g_full[s], kGBytes);
+            tma_load(sG + s * kGBytes, &p.gmap, &g_full[s], 0, 2 * tl.cx0, 2 * tl.cy0, tl.b);
+          }
         }
       } else {
         prefetch_map(&p.vmap);
         prefetch_map(&p.omap);
         uint32_t vc = 0;
-        for (int n = 0; n < local_units && ok; ++n) {
-          const Unit u = unit_of(p, n);
-          const TileXY tl = u.t;
+        for (int n = 0; n < local_tiles && ok; ++n) {
+          const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
           // value window, one ring unit per accumulator half (<= 3 chunks of
           // 64 channels, contiguous so that one MMA spans them)
           for (int h = 0; h < 2 && ok; ++h) {
             const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
-            if (j0 >= j1 || !((u.hmask >> h) & 1)) continue;
+            if (j0 >= j1) continue;
             const int slot = vc % kNU;
             ok = mbar_wait(&v_empty[slot], ((vc / kNU) & 1) ^ 1, abort_flag, 1, tmo);
             if (!ok) break;
@@ -341,23 +365,24 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       auto logits = [&](int n) -> bool {
         const int s = n & 1;
         const uint32_t ph = (n >> 1) & 1;
-        if (!mbar_wait(&g_full[s], ph, abort_flag, 2, tmo)) return false;
+        const int gs = n % kGSlots;
+        if (!mbar_wait(&g_full[gs], (n / kGSlots) & 1, abort_flag, 2, tmo)) return false;
         if (!mbar_wait(&log_empty[s], ph ^ 1, abort_flag, 2, tmo)) return false;
         tc_fence_after();
-        const uint32_t aG = su32(sG + s * kGBytes);
+        const uint32_t aG = su32(sG + gs * kGBytes);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)  // K = 64 guide channels in steps of 16
-          tc_mma(tmem + kLogCol + kLogN * s, mdesc(aG + 32 * k, 16, 1024, kLayoutSw128),
-                 mdesc(aW + 32 * k, 16, 1024, kLayoutSw128), kIdLog, k > 0);
+        for (int src = 0; src < (GF ? 2 : 1); ++src)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)  // K = 64 channels per source in steps of 16
+            tc_mma(tmem + kLogCol + kLogN * s, mdesc(aG + src * kGBytes + 32 * k, 16, 1024, kLayoutSw128),
+                   mdesc(aW + src * kWBytes + 32 * k, 16, 1024, kLayoutSw128), kIdLog, (src | k) > 0);
         tc_commit(&log_full[s]);
-        tc_commit(&g_empty[s]);
+        tc_commit(&g_empty[gs]);
         return true;
       };
-      uint32_t hcnt[2] = {0, 0};  // units so far per accumulator half
-      if (local_units > 0) ok = logits(0);
-      for (int n = 0; n < local_units && ok; ++n) {
-        const int hmask = unit_of(p, n).hmask;
-        if (n + 1 < local_units) {
+      if (local_tiles > 0) ok = logits(0);
+      for (int n = 0; n < local_tiles && ok; ++n) {
+        if (n + 1 < local_tiles) {
           ok = logits(n + 1);
           if (!ok) break;
         }
@@ -371,8 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
         // MMAs of the other
         for (int h = 0; h < 2 && ok; ++h) {
           const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
-          if (j0 >= j1 || !((hmask >> h) & 1)) continue;
-          ok = mbar_wait(&out_empty[h], (hcnt[h] & 1) ^ 1, abort_flag, 2, tmo);
+          if (j0 >= j1) continue;
+          ok = mbar_wait(&out_empty[h], (n & 1) ^ 1, abort_flag, 2, tmo);
           if (!ok) break;
           tc_fence_after();
           const int slot = vc % kNU;
@@ -389,7 +414,6 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
           tc_commit(&v_empty[slot]);
           if (!ok) break;
           tc_commit(&out_full[h]);
-          ++hcnt[h];
         }
         if (!ok) break;
         tc_commit(&a2_empty[s]);
@@ -409,8 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     const int py = i >> 4, px = i & 15;
     const int cr = py >> 1, cc = px >> 1;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-    for (int n = wg; n < local_units; n += 2) {
-      const TileXY tl = unit_of(p, n).t;
+    for (int n = wg; n < local_tiles; n += 2) {
+      const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
       const int s = n & 1;
       const uint32_t ph = (n >> 1) & 1;
       if (!mbar_wait(&log_full[s], ph, abort_flag, 3, tmo)) break;
@@ -421,12 +445,12 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&log_empty[s]);
-      if (!mbar_wait(&g_full[s], ph, abort_flag, 3, tmo)) break;
+      if (!GF && !mbar_wait(&g_full[s], ph, abort_flag, 3, tmo)) break;
 
       float lg[K];
 #pragma unroll
       for (int k = 0; k < K; ++k) lg[k] = __uint_as_float(r[k]) + sBias[k];
-      if (p.res_k > 0) {  // residual_auto: + guide[k] for k < min(K, Cg)
+      if (!GF && p.res_k > 0) {  // residual_auto: + guide[k] for k < min(K, Cg)
         const uint8_t* grow = sG + s * kGBytes + i * 128;
 #pragma unroll
         for (int c8 = 0; c8 < (K + 7) / 8; ++c8) {
@@ -441,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&g_empty[s]);
+      if (!GF && lane == 0) mbar_arrive(&g_empty[s]);
 
       float pk[K];
       if (p.hardmax) {
@@ -512,13 +536,9 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     uint8_t* bufs = sStage + (warp - 10) * 2 * kWarpStage;  // two staging buffers per warp
     uint32_t jw = 0;
     const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
-    uint32_t cnt = 0;  // units of this half so far
-    for (int n = 0; n < local_units && j0 < j1; ++n) {
-      const Unit u = unit_of(p, n);
-      if (!((u.hmask >> h) & 1)) continue;
-      const TileXY tl = u.t;
-      if (!mbar_wait(&out_full[h], cnt & 1, abort_flag, 4, tmo)) break;
-      ++cnt;
+    for (int n = 0; n < local_tiles && j0 < j1; ++n) {
+      const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+      if (!mbar_wait(&out_full[h], n & 1, abort_flag, 4, tmo)) break;
       tc_fence_after();
       for (int j = j0; j < j1; ++j) {
         uint32_t r[64];
@@ -561,30 +581,34 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     // The resize maps 8 input rows / 16 input columns onto exactly 7 / 14
     // output rows / columns (host-checked with the same source-index
     // formula), so a tile's output pixels depend on that tile alone.  Per
-    // 64-channel chunk the warpgroup writes the tile in storage precision
+    // 32-channel step the warpgroup writes the tile in storage precision
     // (rounded as the stored attender output would be) to T, resamples it
-    // to O in fp32 and stores O with one TMA box.  Warps synchronise with
-    // named barriers: one thread waits on the accumulator barrier and
-    // shares the outcome, so all 128 threads always take the same path.
+    // to O in fp32 and one thread stores O with a TMA box.  T and O are
+    // double-buffered: the threads wait for each other once per step (T
+    // complete); only the storing warp also waits for O to be complete.
+    // One thread waits on the accumulator barrier and shares the outcome,
+    // so all 128 threads always take the same path.
     const int q = warp & 3;
     const int h = (warp - 10) >> 2;
     const int t = tid - (10 + 4 * h) * 32;  // thread in the warpgroup
     const bool leader = t == 0;
+    const bool store_warp = q == 0;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-    uint8_t* sT = sStage + h * kRsHalfBytes;
-    uint8_t* sO = sT + kRsTileBytes;
-    volatile int* go = reinterpret_cast<volatile int*>(sO + kRsOutBytes);
+    uint8_t* region = sStage + h * kRsHalfBytes;
+    volatile int* go = reinterpret_cast<volatile int*>(region + kRsOffGo);
     const int bar_t = 1 + h, bar_o = 3 + h;
-    const int oc = t >> 3;  // output column of the tile (< 14) this thread resamples
-    const int cg = t & 7;   // its 16-byte channel group
+    // resampling work of this thread: output column oc of the tile,
+    // 8-channel group cg of the step, output rows [ry0, ry1)
+    const bool worker = t < 2 * kRsOutX * 4;
+    const int cg = t & 3;
+    const int oc = (t >> 2) % kRsOutX;
+    const int ry0 = t < kRsOutX * 4 ? 0 : 4, ry1 = t < kRsOutX * 4 ? 4 : kRsOutY;
     const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
-    uint32_t cnt = 0;  // units of this half so far
-    for (int n = 0; n < local_units && j0 < j1; ++n) {
-      const Unit u = unit_of(p, n);
-      if (!((u.hmask >> h) & 1)) continue;  // the same decision in all 128 threads
-      const TileXY tl = u.t;
-      if (leader) *go = mbar_wait(&out_full[h], cnt & 1, abort_flag, 4, tmo) ? 1 : 0;
-      ++cnt;
+    const int s0 = j0 * (kChunk / kRsChunk), s1 = j1 * (kChunk / kRsChunk);  // 32-channel steps
+    uint32_t step = 0;
+    for (int n = 0; n < local_tiles && s0 < s1; ++n) {
+      const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
+      if (leader) *go = mbar_wait(&out_full[h], n & 1, abort_flag, 4, tmo) ? 1 : 0;
       named_bar(bar_t, 128);
       if (*go == 0) break;
       tc_fence_after();
@@ -594,20 +618,22 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       float lx0 = 0.f, lx1 = 0.f;
       src_coord_bilinear(ox, p.scale_w, p.Wi, x0, xp, lx0, lx1);
       const int xa = min(max(x0 - 2 * tl.cx0, 0), 15), xb = min(xa + xp, 15);
-      for (int j = j0; j < j1; ++j) {
-        // T row of this lane's pixel (TMEM lane = pixel of the tile), read
-        // from TMEM 32 columns at a time
-        uint8_t* trow = sT + (32 * q + lane) * 128;
-#pragma unroll
-        for (int part = 0; part < 2; ++part) {
+      const float2 lx0v = make_float2(lx0, lx0), lx1v = make_float2(lx1, lx1);
+      for (int sj = s0; sj < s1; ++sj, ++step) {
+        const int b = step & 1;
+        uint8_t* sT = region + b * kRsTBytes;
+        uint8_t* sO = region + kRsOffO + b * kRsOSlot;
+        {  // this lane's pixel (TMEM lane = pixel of the tile) into T
           uint32_t r[32];
-          tc_ld32(lane_base + kChunk * j + 32 * part, r);
+          tc_ld32(lane_base + kRsChunk * sj, r);
           tc_wait_ld();
-          if (part == 1 && j + 1 == j1) {  // last TMEM read of this half is complete
+          if (sj + 1 == s1) {  // last TMEM read of this half is complete
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&out_empty[h]);
           }
+          const int row = 32 * q + lane;
+          uint8_t* trow = sT + row * 64;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             const uint32_t* src = r + 8 * c;
@@ -616,30 +642,29 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
             w.y = S::pack(__uint_as_float(src[2]), __uint_as_float(src[3]));
             w.z = S::pack(__uint_as_float(src[4]), __uint_as_float(src[5]));
             w.w = S::pack(__uint_as_float(src[6]), __uint_as_float(src[7]));
-            const int cc = 4 * part + c;
-            *reinterpret_cast<uint4*>(trow + ((cc ^ (lane & 7)) << 4)) = w;
+            *reinterpret_cast<uint4*>(trow + ((c ^ ((row >> 1) & 3)) << 4)) = w;
           }
         }
-        if (leader) bulk_wait_read0();  // the previous chunk's store has read O
-        named_bar(bar_t, 128);
-        if (oc < kRsOutX) {
-          // sweep the 7 output rows: the horizontal interpolation of each
+        if (leader) bulk_wait_read1();  // the store of two steps ago has read this O buffer
+        named_bar(bar_t, 128);          // T complete (and every thread is past step - 1)
+        if (worker) {
+          // sweep the output rows: the horizontal interpolation of each
           // source row is computed once and reused by the next output row
-          float ha[8], hb[8];
+          float2 ha[4], hb[4];
           int ra = -1, rb = -1;
-          auto horiz = [&](int yl, float* dst) {
+          auto horiz = [&](int yl, float2* dst) {
             const int pa = yl * 16 + xa, pb = yl * 16 + xb;
-            const uint4 va = *reinterpret_cast<const uint4*>(sT + pa * 128 + ((cg ^ (pa & 7)) << 4));
-            const uint4 vb = *reinterpret_cast<const uint4*>(sT + pb * 128 + ((cg ^ (pb & 7)) << 4));
+            const uint4 va = *reinterpret_cast<const uint4*>(sT + pa * 64 + ((cg ^ ((pa >> 1) & 3)) << 4));
+            const uint4 vb = *reinterpret_cast<const uint4*>(sT + pb * 64 + ((cg ^ ((pb >> 1) & 3)) << 4));
             const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float a = S::from_bits((uint16_t)(wa[e >> 1] >> ((e & 1) * 16)));
-              const float b = S::from_bits((uint16_t)(wb[e >> 1] >> ((e & 1) * 16)));
-              dst[e] = lx0 * a + lx1 * b;
+            for (int e = 0; e < 4; ++e) {
+              const float2 a = make_float2(S::from_bits((uint16_t)(wa[e] & 0xffffu)), S::from_bits((uint16_t)(wa[e] >> 16)));
+              const float2 c = make_float2(S::from_bits((uint16_t)(wb[e] & 0xffffu)), S::from_bits((uint16_t)(wb[e] >> 16)));
+              dst[e] = __ffma2_rn(lx0v, a, __fmul2_rn(lx1v, c));  // lx0 * a + lx1 * b
             }
           };
-          for (int ry = 0; ry < kRsOutY; ++ry) {
+          for (int ry = ry0; ry < ry1; ++ry) {
             const int oy = kRsOutY * (tl.cy0 / kCellsY) + ry;
             int y0, yp;
             float ly0, ly1;
@@ -648,7 +673,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
             if (ya != ra) {
               if (ya == rb) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) ha[e] = hb[e];
+                for (int e = 0; e < 4; ++e) ha[e] = hb[e];
               } else {
                 horiz(ya, ha);
               }
@@ -657,26 +682,34 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
             if (yb != rb) {
               if (yb == ra) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) hb[e] = ha[e];
+                for (int e = 0; e < 4; ++e) hb[e] = ha[e];
               } else {
                 horiz(yb, hb);
               }
               rb = yb;
             }
+            const float2 ly0v = make_float2(ly0, ly0), ly1v = make_float2(ly1, ly1);
+            float2 o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[e] = __ffma2_rn(ly0v, ha[e], __fmul2_rn(ly1v, hb[e]));
             uint4 w;
-            w.x = S::pack(ly0 * ha[0] + ly1 * hb[0], ly0 * ha[1] + ly1 * hb[1]);
-            w.y = S::pack(ly0 * ha[2] + ly1 * hb[2], ly0 * ha[3] + ly1 * hb[3]);
-            w.z = S::pack(ly0 * ha[4] + ly1 * hb[4], ly0 * ha[5] + ly1 * hb[5]);
-            w.w = S::pack(ly0 * ha[6] + ly1 * hb[6], ly0 * ha[7] + ly1 * hb[7]);
+            w.x = S::pack(o[0].x, o[0].y);
+            w.y = S::pack(o[1].x, o[1].y);
+            w.z = S::pack(o[2].x, o[2].y);
+            w.w = S::pack(o[3].x, o[3].y);
             const int orow = ry * kRsOutX + oc;
-            *reinterpret_cast<uint4*>(sO + orow * 128 + ((cg ^ (orow & 7)) << 4)) = w;
+            *reinterpret_cast<uint4*>(sO + orow * 64 + ((cg ^ ((orow >> 1) & 3)) << 4)) = w;
           }
         }
         fence_proxy_async();
-        named_bar(bar_o, 128);
-        if (leader) {
-          tma_store(&p.omap, sO, j * kChunk, kRsOutX * (tl.cx0 / kCellsX), kRsOutY * (tl.cy0 / kCellsY), tl.b);
-          bulk_commit();
+        if (store_warp) {
+          named_bar(bar_o, 128);  // O complete
+          if (leader) {
+            tma_store(&p.omap, sO, kRsChunk * sj, kRsOutX * (tl.cx0 / kCellsX), kRsOutY * (tl.cy0 / kCellsY), tl.b);
+            bulk_commit();
+          }
+        } else {
+          named_arrive(bar_o, 128);
         }
       }
     }
@@ -711,10 +744,9 @@ EncodeTiled encode_fn() {
 
 }  // namespace tc
 
-// NHWC 4-D map with the 128-byte swizzle: dims {C, W, H, B}, strides in
-// elements of `es` bytes.
+// NHWC 4-D map: dims {C, W, H, B}, strides in elements of `es` bytes.
 int tc_make_map(CUtensorMap* map, CUtensorMapDataType dt, int es, const void* base, int C, int W, int H, int B,
-                int64_t s_w, int64_t s_h, int64_t s_b, int box_c, int box_w, int box_h) {
+                int64_t s_w, int64_t s_h, int64_t s_b, int box_c, int box_w, int box_h, CUtensorMapSwizzle swizzle) {
   tc::EncodeTiled enc = tc::encode_fn();
   if (enc == nullptr) return fail(UPLIFT_LA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)B};
@@ -722,16 +754,16 @@ int tc_make_map(CUtensorMap* map, CUtensorMapDataType dt, int es, const void* ba
   const cuuint32_t box[4] = {(cuuint32_t)box_c, (cuuint32_t)box_w, (cuuint32_t)box_h, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(UPLIFT_LA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return UPLIFT_LA_OK;
 }
 
 namespace tc {
 
-template <typename T, int K, bool RS>
+template <typename T, int K, bool RS, bool GF>
 int launch_t(const Params& p, int dev, int grid, cudaStream_t stream) {
-  auto fn = la_tc_kernel<T, K, RS>;
+  auto fn = la_tc_kernel<T, K, RS, GF>;
   // the shared-memory opt-in is per function and device; set it once (two
   // threads racing here both set the same value, which is harmless)
   static std::atomic<bool> configured[64] = {};
@@ -756,16 +788,22 @@ int launch_t(const Params& p, int dev, int grid, cudaStream_t stream) {
   return UPLIFT_LA_OK;
 }
 
-template <typename T, bool RS>
+template <typename T, bool RS, bool GF>
 int launch_k(const Params& p, int K, int dev, int grid, cudaStream_t stream) {
   switch (K) {
-    case 5: return launch_t<T, 5, RS>(p, dev, grid, stream);
-    case 9: return launch_t<T, 9, RS>(p, dev, grid, stream);
-    case 13: return launch_t<T, 13, RS>(p, dev, grid, stream);
-    case 17: return launch_t<T, 17, RS>(p, dev, grid, stream);
-    case 25: return launch_t<T, 25, RS>(p, dev, grid, stream);
+    case 5: return launch_t<T, 5, RS, GF>(p, dev, grid, stream);
+    case 9: return launch_t<T, 9, RS, GF>(p, dev, grid, stream);
+    case 13: return launch_t<T, 13, RS, GF>(p, dev, grid, stream);
+    case 17: return launch_t<T, 17, RS, GF>(p, dev, grid, stream);
+    case 25: return launch_t<T, 25, RS, GF>(p, dev, grid, stream);
     default: return fail(UPLIFT_LA_ERR_SHAPE, "K=%d unsupported", K);
   }
+}
+
+template <typename T>
+int launch_v(const Params& p, int K, bool rs, bool gf, int dev, int grid, cudaStream_t stream) {
+  if (rs) return gf ? launch_k<T, true, true>(p, K, dev, grid, stream) : launch_k<T, true, false>(p, K, dev, grid, stream);
+  return gf ? launch_k<T, false, true>(p, K, dev, grid, stream) : launch_k<T, false, false>(p, K, dev, grid, stream);
 }
 
 }  // namespace tc
@@ -813,6 +851,12 @@ bool tc_eligible(const TcArgs& a, const char** why) {
   const int64_t st[9] = {a.g_b, a.g_h, a.g_w, a.v_b, a.v_h, a.v_w, a.o_b, a.o_h, a.o_w};
   for (int i = 0; i < 9; ++i)
     if (st[i] % 8 != 0 || st[i] <= 0) return no("strides not multiples of 16 bytes");
+  if (a.guide2 != nullptr) {
+    if (!a16(a.guide2)) return no("residual input not 16-byte aligned");
+    if (a.g2_b % 8 != 0 || a.g2_h % 8 != 0 || a.g2_w % 8 != 0 || a.g2_b <= 0 || a.g2_h <= 0 || a.g2_w <= 0)
+      return no("residual input strides not multiples of 16 bytes");
+    if (a.w_guide == nullptr) return no("no guide block weight");
+  }
   return true;
 }
 
@@ -852,9 +896,12 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
   const bool rs = a.Ho > 0;
   const CUtensorMapDataType dt = a.dtype == UPLIFT_LA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   int rc = tc_make_map(&p.gmap, dt, 2, a.guide, a.Cg, 2 * a.W, 2 * a.H, a.B, a.g_w, a.g_h, a.g_b, 64, 16, 8);
+  if (rc == UPLIFT_LA_OK && a.guide2 != nullptr)
+    rc = tc_make_map(&p.gmap2, dt, 2, a.guide2, a.Cg, 2 * a.W, 2 * a.H, a.B, a.g2_w, a.g2_h, a.g2_b, 64, 16, 8);
   if (rc == UPLIFT_LA_OK) rc = tc_make_map(&p.vmap, dt, 2, a.value, a.C, a.W, a.H, a.B, a.v_w, a.v_h, a.v_b, 64, kWinX, 8);
   if (rc == UPLIFT_LA_OK) {
-    rc = rs ? tc_make_map(&p.omap, dt, 2, a.out, a.C, a.Wo, a.Ho, a.B, a.o_w, a.o_h, a.o_b, 64, kRsOutX, kRsOutY)
+    rc = rs ? tc_make_map(&p.omap, dt, 2, a.out, a.C, a.Wo, a.Ho, a.B, a.o_w, a.o_h, a.o_b, kRsChunk, kRsOutX,
+                          kRsOutY, CU_TENSOR_MAP_SWIZZLE_64B)
             : tc_make_map(&p.omap, dt, 2, a.out, a.C, 2 * a.W, 2 * a.H, a.B, a.o_w, a.o_h, a.o_b, 64, 16, 2);
   }
   if (rc != UPLIFT_LA_OK) return rc;
@@ -878,7 +925,10 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
   const int64_t nt = (int64_t)p.tiles_x * p.tiles_y * a.B;
   if (nt >= (1ll << 31)) return fail(UPLIFT_LA_ERR_SHAPE, "too many tiles");
   p.num_tiles = (int)nt;
-  p.res_k = a.conv_res ? std::min(a.K, a.Cg) : 0;
+  p.res_k = (a.conv_res && a.guide2 == nullptr) ? std::min(a.K, a.Cg) : 0;
+  p.w_guide = a.w_guide;
+  p.b_guide = a.b_guide;
+  p.conv_res = a.conv_res;
   p.timeout_ns = tc_test_timeout_ns() != 0 ? tc_test_timeout_ns() : kTimeoutNs;
   p.host_status = host_status_word();
   p.test_fault = tc_test_fault();
@@ -892,23 +942,10 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (dev >= 0 && dev < 64) sm_count[dev].store(sms, std::memory_order_relaxed);
   }
-  // Grids with few tiles per SM (the first levels of the upsampler) split
-  // every tile into its two accumulator halves, so each CTA pipelines
-  // several units instead of running one or two tiles start to finish.
-  static const int split_below = [] {
-    const char* e = getenv("ULA_TC_SPLIT_TILES_PER_SM");
-    return e != nullptr ? atoi(e) : kSplitTilesPerSm;
-  }();
-  p.split = (p.nchunks >= 2 && nt < (int64_t)split_below * std::max(sms, 1)) ? 1 : 0;
-  const int64_t units = nt * (p.split ? 2 : 1);
-  if (units >= (1ll << 31)) return fail(UPLIFT_LA_ERR_SHAPE, "too many tiles");
-  p.num_units = (int)units;
-  const int grid = (int)std::min<int64_t>(units, std::max(sms, 1));
-  if (rs)
-    return a.dtype == UPLIFT_LA_BF16 ? launch_k<__nv_bfloat16, true>(p, a.K, dev, grid, stream)
-                                     : launch_k<__half, true>(p, a.K, dev, grid, stream);
-  return a.dtype == UPLIFT_LA_BF16 ? launch_k<__nv_bfloat16, false>(p, a.K, dev, grid, stream)
-                                   : launch_k<__half, false>(p, a.K, dev, grid, stream);
+  const int grid = (int)std::min<int64_t>(nt, std::max(sms, 1));
+  const bool gf = a.guide2 != nullptr;
+  return a.dtype == UPLIFT_LA_BF16 ? launch_v<__nv_bfloat16>(p, a.K, rs, gf, dev, grid, stream)
+                                   : launch_v<__half>(p, a.K, rs, gf, dev, grid, stream);
 }
 
 }  // namespace ula

@@ -74,6 +74,11 @@ static __device__ __noinline__ bool mbar_wait_status(uint64_t* b, uint32_t parit
 __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
+// Arrive at a named barrier without waiting (the producer side of a
+// producer / consumer hand-off; the consumers use named_bar).
+__device__ __forceinline__ void named_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -334,6 +334,69 @@ int uplift_la_forward_resized(const void* guide, const int64_t guide_strides[4],
   return rc;
 }
 
+int uplift_la_forward_fused_guide(const void* act, const int64_t act_strides[4],
+                                  const void* res, const int64_t res_strides[4],
+                                  const float* w_guide, const float* b_guide,
+                                  const void* value, const int64_t value_strides[4],
+                                  const float* weight, const float* bias,
+                                  void* out, const int64_t out_strides[4],
+                                  int B, int Cg, int C, int H, int W, int I, int K,
+                                  const int8_t* offsets, int pn, int conv_res,
+                                  int dtype, int hardmax, int Ho, int Wo, void* stream) {
+  using namespace ula;
+  if (dtype != UPLIFT_LA_F32 && dtype != UPLIFT_LA_BF16 && dtype != UPLIFT_LA_F16)
+    return fail(UPLIFT_LA_ERR_ARG, "unknown dtype %d", dtype);
+  if (act_strides == nullptr || res_strides == nullptr || value_strides == nullptr || out_strides == nullptr ||
+      offsets == nullptr)
+    return fail(UPLIFT_LA_ERR_ARG, "null stride or offset array");
+  const bool resize = Ho > 0 || Wo > 0;
+  if (B < 0 || Cg < 1 || C < 1 || H < 0 || W < 0 || I < 1 || (resize && (Ho < 1 || Wo < 1)))
+    return fail(UPLIFT_LA_ERR_SHAPE, "bad sizes B=%d Cg=%d C=%d H=%d W=%d I=%d Ho=%d Wo=%d", B, Cg, C, H, W, I, Ho,
+                Wo);
+  if (K < 1 || K > kMaxK) return fail(UPLIFT_LA_ERR_SHAPE, "K=%d out of range", K);
+  if (pn < 0 || pn > UPLIFT_LA_MAX_PN) return fail(UPLIFT_LA_ERR_OFFSETS, "pn=%d out of range", pn);
+  for (int k = 0; k < K; ++k) {
+    const int dy = offsets[2 * k], dx = offsets[2 * k + 1];
+    if (dy < -pn || dy > pn || dx < -pn || dx > pn)
+      return fail(UPLIFT_LA_ERR_OFFSETS, "offset %d = (%d, %d) exceeds pn=%d", k, dy, dx, pn);
+  }
+  if (act_strides[1] != 1 || res_strides[1] != 1 || value_strides[1] != 1 || out_strides[1] != 1)
+    return fail(UPLIFT_LA_ERR_LAYOUT, "all tensors need channel stride 1 (channels_last)");
+  if (B == 0) return UPLIFT_LA_OK;
+  if (H == 0 || W == 0) return fail(UPLIFT_LA_ERR_SHAPE, "empty value map");
+  if (act == nullptr || res == nullptr || w_guide == nullptr || value == nullptr || weight == nullptr ||
+      out == nullptr)
+    return fail(UPLIFT_LA_ERR_ARG, "null tensor pointer");
+  if (__atomic_load_n(&g_policy, __ATOMIC_RELAXED) == UPLIFT_LA_POLICY_SIMT)
+    return fail(UPLIFT_LA_ERR_UNSUPPORTED, "fused guide needs the tensor-core kernel (policy SIMT)");
+  if (I != 2) return fail(UPLIFT_LA_ERR_UNSUPPORTED, "fused guide: scale I=%d != 2", I);
+  int64_t gs[4] = {act_strides[0], act_strides[1], act_strides[2], act_strides[3]};
+  int64_t rs[4] = {res_strides[0], res_strides[1], res_strides[2], res_strides[3]};
+  int64_t vs[4] = {value_strides[0], value_strides[1], value_strides[2], value_strides[3]};
+  int64_t os[4] = {out_strides[0], out_strides[1], out_strides[2], out_strides[3]};
+  canon_strides(gs, Cg, I * H, I * W, B);
+  canon_strides(rs, Cg, I * H, I * W, B);
+  canon_strides(vs, C, H, W, B);
+  canon_strides(os, C, resize ? Ho : I * H, resize ? Wo : I * W, B);
+  TcArgs a;
+  a.guide = act; a.g_b = gs[0]; a.g_h = gs[2]; a.g_w = gs[3];
+  a.guide2 = res; a.g2_b = rs[0]; a.g2_h = rs[2]; a.g2_w = rs[3];
+  a.w_guide = w_guide; a.b_guide = b_guide;
+  a.value = value; a.v_b = vs[0]; a.v_h = vs[2]; a.v_w = vs[3];
+  a.out = out; a.o_b = os[0]; a.o_h = os[2]; a.o_w = os[3];
+  a.weight = weight; a.bias = bias;
+  a.B = B; a.Cg = Cg; a.C = C; a.H = H; a.W = W; a.K = K; a.pn = pn;
+  a.conv_res = conv_res ? 1 : 0; a.hardmax = hardmax ? 1 : 0; a.dtype = dtype; a.offsets = offsets;
+  if (resize) { a.Ho = Ho; a.Wo = Wo; }
+  const char* why = nullptr;
+  if (!tc_eligible(a, &why) || (resize && !tc_resize_eligible(a, &why)))
+    return fail(UPLIFT_LA_ERR_UNSUPPORTED, "fused guide not applicable: %s", why);
+  const int rc = tc_launch(a, static_cast<cudaStream_t>(stream));
+  if (rc == UPLIFT_LA_OK)
+    g_last_kernel = resize ? UPLIFT_LA_KERNEL_TENSOR_CORE_GUIDE_RESIZE : UPLIFT_LA_KERNEL_TENSOR_CORE_GUIDE;
+  return rc;
+}
+
 int uplift_la_pool(const void* logits, const int64_t logits_strides[4],
                    const void* value, const int64_t value_strides[4],
                    void* out, const int64_t out_strides[4],

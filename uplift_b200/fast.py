@@ -73,6 +73,9 @@ class OptimizedUPLiFT(nn.Module):
         self.model = self.model.to(memory_format=torch.channels_last)
         self._compiled_forward = None
         self.allow_tf32 = None  # set by make_fast
+        # produce the guide inside the attender launch (the decoder's last
+        # 1x1 convolution and residual folded into its projection)
+        self.fuse_guide = True
 
     @torch.inference_mode()
     def forward(self, img, x, outsize=None):
@@ -101,15 +104,22 @@ class OptimizedUPLiFT(nn.Module):
                 enc_feats = _encoder(m.encoder, img_i)
             else:
                 enc_feats = ex_feats
-            x = _decoder(m.decoder, x, enc_feats)
+            wrapped = isinstance(m.attender, AttenderWrapper)
+            # the decoder's last 1x1 convolution + residual (the guide) is
+            # computed inside the attender launch where the kernel allows it
+            x = _decoder(m.decoder, x, enc_feats, defer_guide=wrapped and self.fuse_guide)
             # the last attender call also applies the final resize when
             # nothing runs between the two (one launch, the attender output
             # is never stored)
-            fuse = (outsize is not None and i == m.iters - 1 and m.refiner is None
-                    and isinstance(m.attender, AttenderWrapper))
-            if fuse:
-                return m.attender(x, x_in, size=tuple(outsize))
-            if m.attender is not None:
+            fuse = (outsize is not None and i == m.iters - 1 and m.refiner is None and wrapped)
+            size = tuple(outsize) if fuse else None
+            if isinstance(x, _DeferredGuide):
+                x = m.attender.forward_fused_guide(x.act, x.res, x.conv, x_in, size=size)
+                if fuse:
+                    return x
+            elif fuse:
+                return m.attender(x, x_in, size=size)
+            elif m.attender is not None:
                 x = m.attender(x, x_in)
             if m.refiner is not None:
                 x = _combine(x, enc_feats[m.ref_con], m.ref_ncat_c, m.ref_ncat_s, m.ref_enc_resample)
@@ -308,13 +318,47 @@ def _encoder(e, x):
     return feats
 
 
-def _decoder(d, x, enc_feats):
+class _DeferredGuide:
+    """The guide left as the last block's activation before its final 1x1
+    convolution (`act`), that convolution and the block's residual input
+    (`res`, truncated to the guide's channels by the kernel, as
+    residual_auto does): guide = conv(act) + res[:, :Cg]."""
+
+    def __init__(self, act, conv, res):
+        self.act, self.conv, self.res = act, conv, res
+
+
+def _guide_tail(b, x):
+    """A _DeferredGuide for block `b` on input `x` when the block is a
+    residual conv block (stride 1) ending in a Cg -> Cg 1x1 convolution with
+    bias whose residual input has at least Cg channels; else None."""
+    if not isinstance(b, U._ConvBlock) or not b.residual or b.stride != 1:
+        return None
+    mods = list(b.conv)
+    last = mods[-1] if mods else None
+    if not (_plain_conv(last) and tuple(last.kernel_size) == (1, 1) and tuple(last.stride) == (1, 1)
+            and last.groups == 1 and last.bias is not None and last.in_channels == last.out_channels
+            and x.shape[1] >= last.out_channels):
+        return None
+    act, _ = _conv_seq(mods[:-1], x)
+    return _DeferredGuide(_cl(act), last, x)
+
+
+def _decoder(d, x, enc_feats, defer_guide=False):
     x = _combine(x, enc_feats[-1], d.ncat_c, d.ncat_s, d.enc_resample)
-    x = _group(d.block_0, x)
-    for i in range(1, d.up_steps + 1):
-        x = _up(getattr(d, f"up_{i}"), x)
-        x = _combine(x, enc_feats[-1 - i], d.ncat_c, d.ncat_s, d.enc_resample)
-        x = _group(getattr(d, f"block_{i}"), x)
+    for i in range(d.up_steps + 1):
+        if i > 0:
+            x = _up(getattr(d, f"up_{i}"), x)
+            x = _combine(x, enc_feats[-1 - i], d.ncat_c, d.ncat_s, d.enc_resample)
+        g = getattr(d, f"block_{i}")
+        last = i == d.up_steps
+        if last and defer_guide and d.using_attender and g.count > 0:
+            for b in g.blocks[:-1]:
+                x = _block(b, x)
+            tail = _guide_tail(g.blocks[-1], x)
+            x = tail if tail is not None else _block(g.blocks[-1], x)
+        else:
+            x = _group(g, x)
     if d.using_attender:
         return x
     y = d.outc(x)

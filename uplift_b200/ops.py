@@ -155,6 +155,66 @@ def local_attender_resized_raw(guide: torch.Tensor, value: torch.Tensor, weight:
     return out
 
 
+def _fp32(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    if t is None:
+        return None
+    t = t.detach()
+    return t if (t.dtype == torch.float32 and t.is_contiguous()) else t.to(torch.float32).contiguous()
+
+
+def local_attender_fused_guide_raw(act: torch.Tensor, res: torch.Tensor, w_guide: torch.Tensor,
+                                   b_guide: Optional[torch.Tensor], value: torch.Tensor, weight: torch.Tensor,
+                                   bias: Optional[torch.Tensor], offsets: Sequence, pn: int,
+                                   conv_res: bool = True, hardmax: bool = False,
+                                   size: Optional[Sequence[int]] = None) -> torch.Tensor:
+    """The attender of guide = conv1x1(act; w_guide, b_guide) + res[:, :Cg]
+    (the decoder's last residual block, uplift/uplift.py:152-217), with the
+    guide produced inside the attender launch (uplift_la_forward_fused_guide;
+    `size`: also the final resize).  Where the fused kernel does not apply,
+    the guide is built by the 1x1 convolution and the conv-epilogue kernel
+    and the attender runs on it."""
+    dev = _check_cuda(act, res, value, weight)
+    B, C, H, W = value.shape
+    Cg, Ho_a, Wo_a = act.shape[1], act.shape[2], act.shape[3]
+    I = _scale(Ho_a, Wo_a, H, W)
+    if res.shape[1] < Cg or tuple(res.shape[2:]) != (Ho_a, Wo_a) or res.shape[0] != B:
+        raise ValueError(f"residual input {tuple(res.shape)} does not cover the guide {tuple(act.shape)}")
+    K = len(offsets)
+    wg = _fp32(w_guide).reshape(Cg, -1)
+    if wg.shape[1] != Cg:
+        raise ValueError(f"guide block weight {tuple(w_guide.shape)} is not a {Cg}->{Cg} 1x1 convolution")
+    bg = _fp32(b_guide)
+    w = _fp32(weight).reshape(K, -1)
+    b = _fp32(bias)
+    a = _nhwc(act)
+    r = _nhwc(res)[:, :Cg]
+    v = _nhwc(value)
+    Ho, Wo = (I * H, I * W) if size is None else (int(size[0]), int(size[1]))
+    out = torch.empty((B, C, Ho, Wo), dtype=value.dtype, device=dev, memory_format=torch.channels_last)
+    lib = _native.load()
+    _native.host_status.raise_if_set()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        rc = lib.uplift_la_forward_fused_guide(
+            a.data_ptr(), _native.strides(a), r.data_ptr(), _native.strides(r),
+            wg.data_ptr(), None if bg is None else bg.data_ptr(),
+            v.data_ptr(), _native.strides(v), w.data_ptr(), None if b is None else b.data_ptr(),
+            out.data_ptr(), _native.strides(out), B, Cg, C, H, W, I, K, _native.offsets_array(offsets),
+            int(pn), int(bool(conv_res)), _DTYPES[value.dtype], int(bool(hardmax)),
+            0 if size is None else Ho, 0 if size is None else Wo, stream)
+    if rc == _native.ERR_UNSUPPORTED:
+        import torch.nn.functional as F
+        from . import glue
+        y = F.conv2d(a, w_guide.detach().reshape(Cg, Cg, 1, 1).to(act.dtype)).contiguous(
+            memory_format=torch.channels_last)
+        guide = glue.bias_act_raw_(y, None if b_guide is None else b_guide.detach().to(act.dtype), False, r)
+        if size is None:
+            return local_attender_raw(guide, value, w, b, offsets, pn, conv_res, hardmax)
+        return local_attender_resized_raw(guide, value, w, b, offsets, pn, size, conv_res, hardmax)
+    _native.check(rc, "uplift_la_forward_fused_guide")
+    return out
+
+
 def attender_pool_raw(logits: torch.Tensor, value: torch.Tensor, offsets: Sequence, pn: int,
                       hardmax: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Launch uplift_la_pool on pre-projected logits [B, K, I*H, I*W]."""
@@ -274,6 +334,22 @@ def _(guide, value, weight, bias, offsets, pn, size, conv_res, hardmax):
     return value.new_empty((B, C, int(size[0]), int(size[1]))).contiguous(memory_format=torch.channels_last)
 
 
+@torch.library.custom_op("uplift_b200::local_attender_fused_guide", mutates_args=())
+def _local_attender_fused_guide_op(act: torch.Tensor, res: torch.Tensor, w_guide: torch.Tensor,
+                                   b_guide: Optional[torch.Tensor], value: torch.Tensor, weight: torch.Tensor,
+                                   bias: Optional[torch.Tensor], offsets: list[int], pn: int, conv_res: bool,
+                                   hardmax: bool, size: Optional[list[int]]) -> torch.Tensor:
+    return local_attender_fused_guide_raw(act, res, w_guide, b_guide, value, weight, bias, _pairs(offsets), pn,
+                                          conv_res, hardmax, size)
+
+
+@_local_attender_fused_guide_op.register_fake
+def _(act, res, w_guide, b_guide, value, weight, bias, offsets, pn, conv_res, hardmax, size):
+    B, C = value.shape[0], value.shape[1]
+    Ho, Wo = (act.shape[2], act.shape[3]) if size is None else (int(size[0]), int(size[1]))
+    return value.new_empty((B, C, Ho, Wo)).contiguous(memory_format=torch.channels_last)
+
+
 @torch.library.custom_op("uplift_b200::attender_pool", mutates_args=())
 def _attender_pool_op(logits: torch.Tensor, value: torch.Tensor, offsets: list[int], pn: int,
                       hardmax: bool) -> torch.Tensor:
@@ -299,6 +375,15 @@ def local_attender_resized(guide, value, weight, bias, offsets, pn, size, conv_r
     return torch.ops.uplift_b200.local_attender_resized(guide, value, weight, bias, _offsets_flat(offsets),
                                                         int(pn), [int(size[0]), int(size[1])],
                                                         bool(conv_res), bool(hardmax))
+
+
+def local_attender_fused_guide(act, res, w_guide, b_guide, value, weight, bias, offsets, pn, conv_res=True,
+                               hardmax=False, size=None):
+    """Attender with the guide produced inside the launch (custom op entry;
+    inference only)."""
+    return torch.ops.uplift_b200.local_attender_fused_guide(
+        act, res, w_guide, b_guide, value, weight, bias, _offsets_flat(offsets), int(pn), bool(conv_res),
+        bool(hardmax), None if size is None else [int(size[0]), int(size[1])])
 
 
 def attender_pool(logits, value, offsets, pn, hardmax=False):
