@@ -445,7 +445,7 @@ def run_triton_reference(dev, stream, la, value0, guides, ours_out, ours_ms_step
                     "eager, bf16, same inputs and weights"}
 
 
-def run_fused_resize(dev, stream, peak, reps=5):
+def run_fused_resize(dev, stream, peak, reps=5, images=8):
     """The last attender call of the 1022 px DINOv2 upsampler (B=8, value
     384 x 584^2, guide 64 x 1168^2, bf16) with the final resize to 1022^2:
     the two launches (attender writes 1168^2, the resize kernel reads it back)
@@ -454,7 +454,7 @@ def run_fused_resize(dev, stream, peak, reps=5):
     call: guide + value once + the 1022^2 output."""
     from uplift_b200 import glue, ops
     from uplift_b200.attender import neighbourhood
-    K, B, Cv, side = K_NBR, 8, C, 584
+    K, B, Cv, side = K_NBR, images, C, 584
     offsets, pn = neighbourhood(K)
     g = torch.Generator(device=dev).manual_seed(5)
     cl = torch.channels_last
@@ -484,7 +484,7 @@ def run_fused_resize(dev, stream, peak, reps=5):
     return {"two_launches_ms": round(two, 4), "fused_ms": round(one, 4), "speedup": round(two / one, 3),
             "fused_GB_s": round(algo / one / 1e6, 1), "fused_frac_of_peak": round(algo / one / 1e6 / peak, 4),
             "algo_bytes": int(algo),
-            "shape": "B=8, value 384x584^2 -> attender 1168^2 -> bilinear 1022^2, bf16, K=17"}
+            "shape": f"B={B}, value 384x584^2 -> attender 1168^2 -> bilinear 1022^2, bf16, K=17"}
 
 
 def run_glue_rooflines(dev, stream, peak, reps=5):
@@ -1129,6 +1129,8 @@ def main():
                     help="run only the attender backward pass (profiling captures)")
     ap.add_argument("--only-upsampler", action="store_true",
                     help="run only the whole-upsampler pass (profiling captures)")
+    ap.add_argument("--only-fused-resize", action="store_true",
+                    help="run only the fused attender + final resize timing (profiling captures; --images)")
     ap.add_argument("--images", type=int, default=8,
                     help="images per GPU (default 8; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -1150,6 +1152,10 @@ def main():
         elif args.only_backward:
             dev = torch.device("cuda", local)
             res = {"backward": run_backward(dev, torch.cuda.current_stream(dev), load_peaks()[0], B_PER_GPU)}
+        elif args.only_fused_resize:
+            dev = torch.device("cuda", local)
+            res = {"fused_resize": run_fused_resize(dev, torch.cuda.current_stream(dev), load_peaks()[0],
+                                                    images=B_PER_GPU)}
         elif args.only_upsampler:
             dev = torch.device("cuda", local)
             res = {"upsampler": run_upsampler(dev, torch.cuda.current_stream(dev), world, rank, args, outsize=1022,

@@ -265,19 +265,25 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
   } else {
     // A = weight (+ identity on the first K channels with conv_res): source 0
     // (h) gets A . w_guide, source 1 (u) gets A, the bias gains A . b_guide;
-    // computed in fp32, rounded once to the storage type
-    auto a_of = [&](int n, int j) {
-      return p.weight[n * 64 + j] + ((p.conv_res && j == n) ? 1.f : 0.f);
-    };
+    // computed in fp32 from copies in the (not yet used) A-matrix buffers,
+    // rounded once to the storage type
+    float* sWg = reinterpret_cast<float*>(sA2);  // w_guide [64 out][64 in]
+    float* sAm = sWg + 64 * 64;                  // A [32][64]
+    static_assert((64 * 64 + kLogN * 64) * 4 <= 2 * kA2Bytes, "prologue scratch exceeds the A buffers");
+    for (int i = tid; i < 64 * 64; i += kThreads) sWg[i] = p.w_guide[i];
+    for (int i = tid; i < kLogN * 64; i += kThreads) {
+      const int n = i >> 6, j = i & 63;
+      sAm[i] = n < K ? p.weight[n * 64 + j] + ((p.conv_res && j == n) ? 1.f : 0.f) : 0.f;
+    }
+    __syncthreads();
     for (int idx = tid; idx < 2 * kLogN * 64; idx += kThreads) {
       const int src = idx / (kLogN * 64), n = (idx >> 6) % kLogN, c = idx & 63;
       float w = 0.f;
-      if (n < K) {
-        if (src == 1) {
-          w = a_of(n, c);
-        } else {
-          for (int j = 0; j < 64; ++j) w = fmaf(a_of(n, j), p.w_guide[j * 64 + c], w);
-        }
+      if (src == 1) {
+        w = sAm[n * 64 + c];
+      } else {
+#pragma unroll 16
+        for (int j = 0; j < 64; ++j) w = fmaf(sAm[n * 64 + j], sWg[j * 64 + c], w);
       }
       *reinterpret_cast<uint16_t*>(sW + src * kWBytes + n * 128 + ((((c >> 3) ^ (n & 7)) << 4)) + (c & 7) * 2) =
           S::bits(w);
@@ -287,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       if (k < K) {
         bk = p.bias != nullptr ? p.bias[k] : 0.f;
         if (p.b_guide != nullptr)
-          for (int j = 0; j < 64; ++j) bk = fmaf(a_of(k, j), p.b_guide[j], bk);
+          for (int j = 0; j < 64; ++j) bk = fmaf(sAm[k * 64 + j], p.b_guide[j], bk);
       }
       sBias[k] = bk;
     }
