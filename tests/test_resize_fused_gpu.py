@@ -135,8 +135,13 @@ def test_fast_mode_upsampler_uses_the_fused_resize(cuda_lib):
     img = torch.rand(2, 3, 224, 224, generator=g).to(DEV, torch.bfloat16)
     feats = torch.randn(2, 384, 16, 16, generator=g).to(DEV, torch.bfloat16)
     full = fast(img, feats)                       # 64 x 64, no resize
-    out = fast(img, feats, (56, 56))              # 64 -> 56 = 7/8: fused
-    assert _native.last_kernel() == _native.KERNEL_TENSOR_CORE_RESIZE
+    out = fast(img, feats, (56, 56))              # 64 -> 56 = 7/8: fused (with the guide fused too)
+    assert _native.last_kernel() == _native.KERNEL_TENSOR_CORE_GUIDE_RESIZE
+    fast.fuse_guide = False
+    assert _ulp_close(fast(img, feats, (56, 56)), glue.resize_bilinear(fast(img, feats), (56, 56)),
+                      torch.bfloat16)
+    assert _native.last_kernel() == _native.KERNEL_TENSOR_CORE  # the plain call ran last
+    fast.fuse_guide = True
     exp = glue.resize_bilinear(full, (56, 56))
     assert out.shape == (2, 384, 56, 56)
     assert _ulp_close(out, exp, torch.bfloat16)

@@ -101,16 +101,17 @@ constexpr int kWarpStage = 32 * 128;         // 4 KB: one epilogue warp's 32 px 
 constexpr int kOffMisc = kOffBar + kNumBars * 8;   // tmem slot, abort flag
 // Fused final resize (RS kernels): each epilogue warpgroup uses its half of
 // the staging region for two buffers T of one 8 x 16-pixel, 32-channel
-// slice of the tile in storage precision and two buffers O of the 7 x 14
-// resized pixels made from it (laid out as the TMA store box {32, 14, 7}
-// with the 64-byte swizzle: 16-byte chunk c of 64-byte row r sits at
-// chunk c ^ ((r >> 1) & 3); T uses the same layout).
+// slice of the tile in storage precision (64-byte pixel rows; 16-byte chunk
+// c of row r sits at chunk c ^ ((r >> 1) & 3), so a warp's row writes are
+// free of bank conflicts) and two buffers O of the 7 x 14 resized pixels
+// made from it, laid out densely as the TMA store box {32, 14, 7} (a warp
+// writes 8 consecutive 64-byte rows, conflict-free without a swizzle).
 constexpr int kRsHalfBytes = 2 * kStageBytes;           // 32 KB per warpgroup
 constexpr int kRsChunk = 32;                            // channels per resize step
 constexpr int kRsTBytes = kM * 64;                      // T: 8 KB
 constexpr int kRsOutY = 7, kRsOutX = 14;                // resized pixels per tile
 constexpr int kRsOBytes = kRsOutY * kRsOutX * 64;       // O: 6272 B
-constexpr int kRsOSlot = 7 * 1024;                      // O slots 1024-aligned (swizzle atom)
+constexpr int kRsOSlot = 7 * 1024;                      // O slots, 1024-aligned
 constexpr int kRsOffO = 2 * kRsTBytes;
 constexpr int kRsOffGo = kRsOffO + 2 * kRsOSlot;
 static_assert(kRsOBytes <= kRsOSlot && kRsOffGo + 16 <= kRsHalfBytes, "resize staging exceeds the half region");
@@ -598,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     const int h = (warp - 10) >> 2;
     const int t = tid - (10 + 4 * h) * 32;  // thread in the warpgroup
     const bool leader = t == 0;
-    const bool store_warp = q == 0;
+    const bool store_warp = (t >> 5) == 0;  // the warp of the storing thread
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
     uint8_t* region = sStage + h * kRsHalfBytes;
     volatile int* go = reinterpret_cast<volatile int*>(region + kRsOffGo);
@@ -703,8 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
             w.y = S::pack(o[1].x, o[1].y);
             w.z = S::pack(o[2].x, o[2].y);
             w.w = S::pack(o[3].x, o[3].y);
-            const int orow = ry * kRsOutX + oc;
-            *reinterpret_cast<uint4*>(sO + orow * 64 + ((cg ^ ((orow >> 1) & 3)) << 4)) = w;
+            *reinterpret_cast<uint4*>(sO + (ry * kRsOutX + oc) * 64 + cg * 16) = w;
           }
         }
         fence_proxy_async();
@@ -907,7 +907,7 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
   if (rc == UPLIFT_LA_OK) rc = tc_make_map(&p.vmap, dt, 2, a.value, a.C, a.W, a.H, a.B, a.v_w, a.v_h, a.v_b, 64, kWinX, 8);
   if (rc == UPLIFT_LA_OK) {
     rc = rs ? tc_make_map(&p.omap, dt, 2, a.out, a.C, a.Wo, a.Ho, a.B, a.o_w, a.o_h, a.o_b, kRsChunk, kRsOutX,
-                          kRsOutY, CU_TENSOR_MAP_SWIZZLE_64B)
+                          kRsOutY, CU_TENSOR_MAP_SWIZZLE_NONE)
             : tc_make_map(&p.omap, dt, 2, a.out, a.C, 2 * a.W, 2 * a.H, a.B, a.o_w, a.o_h, a.o_b, 64, 16, 2);
   }
   if (rc != UPLIFT_LA_OK) return rc;
