@@ -100,9 +100,12 @@ def test_fused_guide_with_fused_resize(cuda_lib):
 
 def test_fused_guide_falls_back_where_the_kernel_does_not_apply(cuda_lib):
     """fp32 (no tensor-core kernel for a 64-channel fp32 guide): the guide is
-    built by the convolution + epilogue and the attender runs on it."""
+    built by the convolution + epilogue and the attender runs on it (the
+    convolution with TF32 off, as the fp32-exact fast mode runs it)."""
+    from uplift_b200.uplift import tf32_mode
     c = _case(1, 5, 6, 48, 17, torch.float32, seed=9)
-    out = _fused(c)
+    with tf32_mode(False):
+        out = _fused(c)
     assert _native.last_kernel() in _native.KERNELS_CUDA_CORE
     assert normwise_err(out, _oracle(c)) <= TOL[torch.float32]
 

@@ -95,7 +95,7 @@ extern "C" int uplift_la_backward(const void* dout, const int64_t dout_strides[4
   const bool gvec = Cg % ve == 0 && a16(guide) && a.g_b % ve == 0 && a.g_h % ve == 0 && a.g_w % ve == 0;
   // sliding-window dV when the offsets are the reference's table for K; row
   // segments sized so that about 2048 threads per SM are busy
-  bwd::Plan plan{0, 0, W, 1};
+  bwd::Plan plan{0, 0, 0, W, 1};
   {
     // tensor-core dlogit: I = 2, even Cg <= 64, C % 32 == 0 (16-bit storage)
     // or C % 16 == 0 (fp32), 16-byte dout / value rows, aligned guide / dguide
@@ -142,6 +142,22 @@ extern "C" int uplift_la_backward(const void* dout, const int64_t dout_strides[4
     if (nseg > 1 && (W + nseg - 1) / nseg < min_len) nseg = std::max(1, W / min_len);
     plan.seg_len = (W + nseg - 1) / nseg;
     plan.nseg = (W + plan.seg_len - 1) / plan.seg_len;
+  }
+  if (dvalue != nullptr && dtype != UPLIFT_LA_F32) {
+    // tensor-core dV: I = 2, 16-bit storage, C a multiple of 64 up to 384,
+    // offsets within +-2, aligned NHWC dout / dvalue (ULA_BWD_DV_TC=0 keeps
+    // the CUDA-core kernels, for comparisons)
+    static const bool dv_env = [] {
+      const char* e = getenv("ULA_BWD_DV_TC");
+      return e == nullptr || atoi(e) != 0;
+    }();
+    DvArgs d;
+    d.dout = dout; d.d_b = a.d_b; d.d_h = a.d_h; d.d_w = a.d_w;
+    d.probs = probs;
+    d.dvalue = dvalue; d.dv_b = a.dv_b; d.dv_h = a.dv_h; d.dv_w = a.dv_w;
+    d.B = B; d.C = C; d.H = H; d.W = W; d.I = I; d.K = K; d.dtype = dtype;
+    for (int k = 0; k < K; ++k) { d.dy[k] = a.dy[k]; d.dx[k] = a.dx[k]; }
+    plan.dv_tc = (dv_env && dv_tc_eligible(d, nullptr)) ? 1 : 0;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {

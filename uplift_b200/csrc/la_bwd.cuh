@@ -919,6 +919,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) dlogit_mma_kernel(const Arg
 
 struct Plan {
   int mma_pn;    // 1 or 2: tensor-core dlogit (dlogit_mma_kernel<PN>); 0: CUDA-core dlogit
+  int dv_tc;     // 1: tensor-core dV (la_bwd_dv.cu)
   int window;    // 1: sliding-window dV (reference offset table); 0: general dV kernel
   int seg_len;   // value columns per window thread
   int nseg;
@@ -971,7 +972,17 @@ int launch_cv(const Args& a, const Plan& plan, cudaStream_t stream) {
     dlogit_kernel<T, K, CPT, VEC><<<(unsigned)dblocks, kDThreads, smem_d, stream>>>(a);
   }
   if (a.dvalue != nullptr && a.B * (int64_t)a.H > 0) {
-    if (plan.window) {
+    if (plan.dv_tc) {
+      DvArgs d;
+      d.dout = a.dout; d.d_b = a.d_b; d.d_h = a.d_h; d.d_w = a.d_w;
+      d.probs = a.probs;
+      d.dvalue = a.dvalue; d.dv_b = a.dv_b; d.dv_h = a.dv_h; d.dv_w = a.dv_w;
+      d.B = a.B; d.C = a.C; d.H = a.H; d.W = a.W; d.I = a.I; d.K = K;
+      d.dtype = std::is_same<T, __nv_bfloat16>::value ? UPLIFT_LA_BF16 : UPLIFT_LA_F16;
+      for (int k = 0; k < K; ++k) { d.dy[k] = a.dy[k]; d.dx[k] = a.dx[k]; }
+      const int rc = dv_tc_launch(d, stream);
+      if (rc != UPLIFT_LA_OK) return rc;
+    } else if (plan.window) {
       const int64_t threads = (int64_t)a.B * a.H * plan.nseg * (a.C / VEC);
       const int64_t blocks = (threads + kThreads - 1) / kThreads;
       if (blocks >= (1ll << 31)) return fail(UPLIFT_LA_ERR_SHAPE, "backward: grid too large");

@@ -61,6 +61,19 @@ int tcw_device_status(bool clear);
 // launch so that an expired wait is also written there.
 unsigned int* host_status_word();
 
+// Tensor-core dV of the backward (la_bwd_dv.cu): dvalue from dout and the
+// fp32 softmax workspace; strides in elements, channel stride 1 (NHWC).
+struct DvArgs {
+  const void* dout;   int64_t d_b, d_h, d_w;
+  const float* probs;  // [B][I*H][I*W][K]
+  void* dvalue;       int64_t dv_b, dv_h, dv_w;
+  int B, C, H, W, I, K, dtype;
+  int8_t dy[25], dx[25];
+};
+bool dv_tc_eligible(const DvArgs& a, const char** why);
+int dv_tc_launch(const DvArgs& a, cudaStream_t stream);
+int dv_device_status(bool clear);
+
 // Record an error message for uplift_la_last_error().
 int fail(int code, const char* fmt, ...);
 

@@ -435,8 +435,9 @@ int uplift_la_last_kernel(void) { return ula::g_last_kernel; }
 int uplift_la_device_status(int clear) {
   const int a = ula::tc_device_status(clear != 0);
   const int b = ula::tcw_device_status(clear != 0);
-  if (a < 0 || b < 0) return -1;
-  return a != 0 ? a : b;
+  const int c = ula::dv_device_status(clear != 0);
+  if (a < 0 || b < 0 || c < 0) return -1;
+  return a != 0 ? a : (b != 0 ? b : c);
 }
 
 int uplift_la_set_host_status_word(unsigned int* word) {
