@@ -475,9 +475,9 @@ def run_fused_resize(dev, stream, peak, reps=5, images=8):
             ts.append(e0.elapsed_time(e1))
         return statistics.median(ts)
 
-    with torch.cuda.stream(stream):
-        two = timed(lambda: glue.resize_bilinear(ops.local_attender_raw(guide, value, w, b, offsets, pn), (1022, 1022)))
+    with torch.cuda.stream(stream):  # the fused call first: it is the first attender launch of a capture
         one = timed(lambda: ops.local_attender_resized_raw(guide, value, w, b, offsets, pn, (1022, 1022)))
+        two = timed(lambda: glue.resize_bilinear(ops.local_attender_raw(guide, value, w, b, offsets, pn), (1022, 1022)))
     del guide, value
     torch.cuda.empty_cache()
     algo = B * (2 * side) ** 2 * (CG * ELEM + Cv * ELEM / 4) + B * 1022 * 1022 * Cv * ELEM

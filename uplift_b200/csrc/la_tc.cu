@@ -49,6 +49,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <type_traits>
 
 #include "uplift_la.h"
 #include "la_internal.h"
@@ -609,103 +610,108 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     const bool worker = t < 2 * kRsOutX * 4;
     const int cg = t & 3;
     const int oc = (t >> 2) % kRsOutX;
-    const int ry0 = t < kRsOutX * 4 ? 0 : 4, ry1 = t < kRsOutX * 4 ? 4 : kRsOutY;
+    const int ry0 = t < kRsOutX * 4 ? 0 : 4;  // output rows 0-3, or 4-6
     const int j0 = h * half_chunks, j1 = min(p.nchunks, j0 + half_chunks);
     const int s0 = j0 * (kChunk / kRsChunk), s1 = j1 * (kChunk / kRsChunk);  // 32-channel steps
     uint32_t step = 0;
+    // the lane's pixel (TMEM lane = pixel of the tile) of one 32-channel
+    // step into T, rounded to the storage type
+    auto to_t = [&](uint8_t* sT, const uint32_t* r) {
+      const int row = 32 * q + lane;
+      uint8_t* trow = sT + row * 64;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t* src = r + 8 * c;
+        uint4 w;
+        w.x = S::pack(__uint_as_float(src[0]), __uint_as_float(src[1]));
+        w.y = S::pack(__uint_as_float(src[2]), __uint_as_float(src[3]));
+        w.z = S::pack(__uint_as_float(src[4]), __uint_as_float(src[5]));
+        w.w = S::pack(__uint_as_float(src[6]), __uint_as_float(src[7]));
+        *reinterpret_cast<uint4*>(trow + ((c ^ ((row >> 1) & 3)) << 4)) = w;
+      }
+    };
     for (int n = 0; n < local_tiles && s0 < s1; ++n) {
       const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
       if (leader) *go = mbar_wait(&out_full[h], n & 1, abort_flag, 4, tmo) ? 1 : 0;
       named_bar(bar_t, 128);
       if (*go == 0) break;
       tc_fence_after();
-      // source columns of this thread's output column (same for every row)
+      // this thread's output column: source columns xa, xa + 1 of the tile
+      // (the 7-of-8 pattern the host checked) and PyTorch's fp32 weights
       const int ox = kRsOutX * (tl.cx0 / kCellsX) + oc;
       int x0 = 0, xp = 0;
       float lx0 = 0.f, lx1 = 0.f;
       src_coord_bilinear(ox, p.scale_w, p.Wi, x0, xp, lx0, lx1);
-      const int xa = min(max(x0 - 2 * tl.cx0, 0), 15), xb = min(xa + xp, 15);
+      const int xa = oc + (oc >= 7 ? 1 : 0);
       const float2 lx0v = make_float2(lx0, lx0), lx1v = make_float2(lx1, lx1);
+      uint32_t r[32];
+      tc_ld32(lane_base + kRsChunk * s0, r);
+      tc_wait_ld_regs(r);
+      if (s0 + 1 == s1) {  // last TMEM read of this half is complete
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&out_empty[h]);
+      }
+      to_t(region + (step & 1) * kRsTBytes, r);
       for (int sj = s0; sj < s1; ++sj, ++step) {
         const int b = step & 1;
-        uint8_t* sT = region + b * kRsTBytes;
+        const uint8_t* sT = region + b * kRsTBytes;
         uint8_t* sO = region + kRsOffO + b * kRsOSlot;
-        {  // this lane's pixel (TMEM lane = pixel of the tile) into T
-          uint32_t r[32];
-          tc_ld32(lane_base + kRsChunk * sj, r);
-          tc_wait_ld();
-          if (sj + 1 == s1) {  // last TMEM read of this half is complete
+        if (leader) bulk_wait_read1();  // the store of two steps ago has read this O buffer
+        named_bar(bar_t, 128);          // T complete (and every thread is past step - 1)
+        const bool more = sj + 1 < s1;
+        if (more) tc_ld32(lane_base + kRsChunk * (sj + 1), r);  // lands while this step resamples
+        if (worker) {
+          // horizontal interpolation of the source rows this thread needs
+          // (all loads first), then the vertical one per output row
+          auto sweep = [&](auto r0c, auto nrc) {
+            constexpr int R0 = decltype(r0c)::value, NR = decltype(nrc)::value;
+            uint4 va[NR + 1], vb[NR + 1];
+#pragma unroll
+            for (int i = 0; i <= NR; ++i) {
+              const int pa = (R0 + i) * 16 + xa, pb = pa + 1;
+              va[i] = *reinterpret_cast<const uint4*>(sT + pa * 64 + ((cg ^ ((pa >> 1) & 3)) << 4));
+              vb[i] = *reinterpret_cast<const uint4*>(sT + pb * 64 + ((cg ^ ((pb >> 1) & 3)) << 4));
+            }
+            float2 hr[NR + 1][4];
+#pragma unroll
+            for (int i = 0; i <= NR; ++i) {
+              const uint32_t wa[4] = {va[i].x, va[i].y, va[i].z, va[i].w};
+              const uint32_t wb[4] = {vb[i].x, vb[i].y, vb[i].z, vb[i].w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 a2 = make_float2(S::from_bits((uint16_t)(wa[e] & 0xffffu)), S::from_bits((uint16_t)(wa[e] >> 16)));
+                const float2 b2 = make_float2(S::from_bits((uint16_t)(wb[e] & 0xffffu)), S::from_bits((uint16_t)(wb[e] >> 16)));
+                hr[i][e] = __ffma2_rn(lx0v, a2, __fmul2_rn(lx1v, b2));  // lx0 * a + lx1 * b
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < NR; ++i) {
+              const int oy = kRsOutY * (tl.cy0 / kCellsY) + R0 + i;
+              int y0, yp;
+              float ly0, ly1;
+              src_coord_bilinear(oy, p.scale_h, p.Hi, y0, yp, ly0, ly1);
+              const float2 ly0v = make_float2(ly0, ly0), ly1v = make_float2(ly1, ly1);
+              uint32_t o[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 v = __ffma2_rn(ly0v, hr[i][e], __fmul2_rn(ly1v, hr[i + 1][e]));
+                o[e] = S::pack(v.x, v.y);
+              }
+              *reinterpret_cast<uint4*>(sO + ((R0 + i) * kRsOutX + oc) * 64 + cg * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          };
+          if (ry0 == 0) sweep(std::integral_constant<int, 0>{}, std::integral_constant<int, 4>{});
+          else sweep(std::integral_constant<int, 4>{}, std::integral_constant<int, 3>{});
+        }
+        if (more) {
+          tc_wait_ld_regs(r);
+          if (sj + 2 == s1) {  // last TMEM read of this half is complete
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&out_empty[h]);
           }
-          const int row = 32 * q + lane;
-          uint8_t* trow = sT + row * 64;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint32_t* src = r + 8 * c;
-            uint4 w;
-            w.x = S::pack(__uint_as_float(src[0]), __uint_as_float(src[1]));
-            w.y = S::pack(__uint_as_float(src[2]), __uint_as_float(src[3]));
-            w.z = S::pack(__uint_as_float(src[4]), __uint_as_float(src[5]));
-            w.w = S::pack(__uint_as_float(src[6]), __uint_as_float(src[7]));
-            *reinterpret_cast<uint4*>(trow + ((c ^ ((row >> 1) & 3)) << 4)) = w;
-          }
-        }
-        if (leader) bulk_wait_read1();  // the store of two steps ago has read this O buffer
-        named_bar(bar_t, 128);          // T complete (and every thread is past step - 1)
-        if (worker) {
-          // sweep the output rows: the horizontal interpolation of each
-          // source row is computed once and reused by the next output row
-          float2 ha[4], hb[4];
-          int ra = -1, rb = -1;
-          auto horiz = [&](int yl, float2* dst) {
-            const int pa = yl * 16 + xa, pb = yl * 16 + xb;
-            const uint4 va = *reinterpret_cast<const uint4*>(sT + pa * 64 + ((cg ^ ((pa >> 1) & 3)) << 4));
-            const uint4 vb = *reinterpret_cast<const uint4*>(sT + pb * 64 + ((cg ^ ((pb >> 1) & 3)) << 4));
-            const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 a = make_float2(S::from_bits((uint16_t)(wa[e] & 0xffffu)), S::from_bits((uint16_t)(wa[e] >> 16)));
-              const float2 c = make_float2(S::from_bits((uint16_t)(wb[e] & 0xffffu)), S::from_bits((uint16_t)(wb[e] >> 16)));
-              dst[e] = __ffma2_rn(lx0v, a, __fmul2_rn(lx1v, c));  // lx0 * a + lx1 * b
-            }
-          };
-          for (int ry = ry0; ry < ry1; ++ry) {
-            const int oy = kRsOutY * (tl.cy0 / kCellsY) + ry;
-            int y0, yp;
-            float ly0, ly1;
-            src_coord_bilinear(oy, p.scale_h, p.Hi, y0, yp, ly0, ly1);
-            const int ya = min(max(y0 - 2 * tl.cy0, 0), 7), yb = min(ya + yp, 7);
-            if (ya != ra) {
-              if (ya == rb) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) ha[e] = hb[e];
-              } else {
-                horiz(ya, ha);
-              }
-              ra = ya;
-            }
-            if (yb != rb) {
-              if (yb == ra) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) hb[e] = ha[e];
-              } else {
-                horiz(yb, hb);
-              }
-              rb = yb;
-            }
-            const float2 ly0v = make_float2(ly0, ly0), ly1v = make_float2(ly1, ly1);
-            float2 o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) o[e] = __ffma2_rn(ly0v, ha[e], __fmul2_rn(ly1v, hb[e]));
-            uint4 w;
-            w.x = S::pack(o[0].x, o[0].y);
-            w.y = S::pack(o[1].x, o[1].y);
-            w.z = S::pack(o[2].x, o[2].y);
-            w.w = S::pack(o[3].x, o[3].y);
-            *reinterpret_cast<uint4*>(sO + (ry * kRsOutX + oc) * 64 + cg * 16) = w;
-          }
+          to_t(region + (b ^ 1) * kRsTBytes, r);  // read in step - 1, which every thread has finished
         }
         fence_proxy_async();
         if (store_warp) {
@@ -878,19 +884,23 @@ bool tc_resize_eligible(const TcArgs& a, const char** why) {
   // every output row / column must read its two source rows / columns from
   // the 8 / 16 of its own tile (PyTorch's source-index formula, fp32)
   const float sh = (float)Hi / (float)a.Ho, sw = (float)Wi / (float)a.Wo;
+  // (exactly: output row 7m + r reads input rows 8m + r and 8m + r + 1, and
+  // output column 14m + c reads 16m + c + (c >= 7) and the one after -- the
+  // fixed pattern the kernel's resampling is unrolled for)
   for (int d = 0; d < a.Ho; ++d) {
     int i0, ip;
     float l0, l1;
     src_coord_bilinear(d, sh, Hi, i0, ip, l0, l1);
-    const int base = (d / kRsOutY) * 2 * kCellsY;
-    if (i0 < base || i0 + ip > base + 2 * kCellsY - 1) return no("a resized row reads outside its tile");
+    const int r = d % kRsOutY;
+    if (i0 != (d / kRsOutY) * 2 * kCellsY + r || ip != 1) return no("a resized row does not read rows r, r + 1 of its tile");
   }
   for (int d = 0; d < a.Wo; ++d) {
     int i0, ip;
     float l0, l1;
     src_coord_bilinear(d, sw, Wi, i0, ip, l0, l1);
-    const int base = (d / kRsOutX) * 2 * kCellsX;
-    if (i0 < base || i0 + ip > base + 2 * kCellsX - 1) return no("a resized column reads outside its tile");
+    const int c = d % kRsOutX;
+    if (i0 != (d / kRsOutX) * 2 * kCellsX + c + (c >= 7 ? 1 : 0) || ip != 1)
+      return no("a resized column does not read its tile's columns in the 7-of-8 pattern");
   }
   return true;
 }
