@@ -104,18 +104,13 @@ constexpr int kOffMisc = kOffBar + kNumBars * 8;   // tmem slot, abort flag
 // the staging region for two buffers T of one 8 x 16-pixel, 32-channel
 // slice of the tile in storage precision (64-byte pixel rows; 16-byte chunk
 // c of row r sits at chunk c ^ ((r >> 1) & 3), so a warp's row writes are
-// free of bank conflicts) and two buffers O of the 7 x 14 resized pixels
-// made from it, laid out densely as the TMA store box {32, 14, 7} (a warp
-// writes 8 consecutive 64-byte rows, conflict-free without a swizzle).
+// free of bank conflicts); the resized pixels go straight to global memory.
 constexpr int kRsHalfBytes = 2 * kStageBytes;           // 32 KB per warpgroup
 constexpr int kRsChunk = 32;                            // channels per resize step
 constexpr int kRsTBytes = kM * 64;                      // T: 8 KB
 constexpr int kRsOutY = 7, kRsOutX = 14;                // resized pixels per tile
-constexpr int kRsOBytes = kRsOutY * kRsOutX * 64;       // O: 6272 B
-constexpr int kRsOSlot = 7 * 1024;                      // O slots, 1024-aligned
-constexpr int kRsOffO = 2 * kRsTBytes;
-constexpr int kRsOffGo = kRsOffO + 2 * kRsOSlot;
-static_assert(kRsOBytes <= kRsOSlot && kRsOffGo + 16 <= kRsHalfBytes, "resize staging exceeds the half region");
+constexpr int kRsOffGo = 2 * kRsTBytes;
+static_assert(kRsOffGo + 16 <= kRsHalfBytes, "resize staging exceeds the half region");
 constexpr int kOffBias = kOffMisc + 16;
 constexpr int kSmemBytes = kOffBias + kLogN * 4 + 1024;  // + base alignment slack
 
@@ -144,9 +139,10 @@ struct Params {
   unsigned int* host_status;  // host-visible status word or null
   int test_fault;       // 1: the guide producer issues no loads (tests the timeout path)
   // fused final resize (RS kernels): the attender output [2H, 2W] is never
-  // stored; omap describes the resized output [Ho, Wo] (box {64, 14, 7}).
+  // stored; the resized output [Ho, Wo] is written by plain stores.
   int Hi, Wi;           // attender output size (2H, 2W)
   float scale_h, scale_w;  // Hi / Ho, Wi / Wo (align_corners=False)
+  void* rs_out; int64_t rs_b, rs_h, rs_w;  // the resized output, element strides (channel stride 1)
 };
 
 // Bounded mbarrier wait recording expiries in this kernel's status word.
@@ -160,6 +156,10 @@ template <> struct Store<__nv_bfloat16> {
   static constexpr uint32_t kFmt = 1;
   __device__ __forceinline__ static uint16_t bits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
   __device__ __forceinline__ static float from_bits(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+  // the two values of a packed pair (low half first) as fp32
+  __device__ __forceinline__ static float2 unpack2(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  }
   __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -170,6 +170,9 @@ template <> struct Store<__half> {
   static constexpr uint32_t kFmt = 0;
   __device__ __forceinline__ static uint16_t bits(float x) { return __half_as_ushort(__float2half_rn(x)); }
   __device__ __forceinline__ static float from_bits(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+  __device__ __forceinline__ static float2 unpack2(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  }
   __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -590,21 +593,20 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     // output rows / columns (host-checked with the same source-index
     // formula), so a tile's output pixels depend on that tile alone.  Per
     // 32-channel step the warpgroup writes the tile in storage precision
-    // (rounded as the stored attender output would be) to T, resamples it
-    // to O in fp32 and one thread stores O with a TMA box.  T and O are
+    // (rounded as the stored attender output would be) to T, and 112 of its
+    // threads resample it in fp32, each storing one output column x 8
+    // channels over 3-4 rows straight to global memory.  T is
     // double-buffered: the threads wait for each other once per step (T
-    // complete); only the storing warp also waits for O to be complete.
-    // One thread waits on the accumulator barrier and shares the outcome,
-    // so all 128 threads always take the same path.
+    // complete).  One thread waits on the accumulator barrier and shares the
+    // outcome, so all 128 threads always take the same path.
     const int q = warp & 3;
     const int h = (warp - 10) >> 2;
     const int t = tid - (10 + 4 * h) * 32;  // thread in the warpgroup
     const bool leader = t == 0;
-    const bool store_warp = (t >> 5) == 0;  // the warp of the storing thread
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
     uint8_t* region = sStage + h * kRsHalfBytes;
     volatile int* go = reinterpret_cast<volatile int*>(region + kRsOffGo);
-    const int bar_t = 1 + h, bar_o = 3 + h;
+    const int bar_t = 1 + h;
     // resampling work of this thread: output column oc of the tile,
     // 8-channel group cg of the step, output rows [ry0, ry1)
     const bool worker = t < 2 * kRsOutX * 4;
@@ -616,19 +618,17 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
     uint32_t step = 0;
     // the lane's pixel (TMEM lane = pixel of the tile) of one 32-channel
     // step into T, rounded to the storage type
-    auto to_t = [&](uint8_t* sT, const uint32_t* r) {
+    auto pack32 = [&](const uint32_t* r, uint32_t* pk) {  // 32 fp32 -> 16 words of 2 storage values
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pk[i] = S::pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+    };
+    auto to_t = [&](uint8_t* sT, const uint32_t* pk) {
       const int row = 32 * q + lane;
       uint8_t* trow = sT + row * 64;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint32_t* src = r + 8 * c;
-        uint4 w;
-        w.x = S::pack(__uint_as_float(src[0]), __uint_as_float(src[1]));
-        w.y = S::pack(__uint_as_float(src[2]), __uint_as_float(src[3]));
-        w.z = S::pack(__uint_as_float(src[4]), __uint_as_float(src[5]));
-        w.w = S::pack(__uint_as_float(src[6]), __uint_as_float(src[7]));
-        *reinterpret_cast<uint4*>(trow + ((c ^ ((row >> 1) & 3)) << 4)) = w;
-      }
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(trow + ((c ^ ((row >> 1) & 3)) << 4)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
     };
     for (int n = 0; n < local_tiles && s0 < s1; ++n) {
       const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
@@ -644,88 +644,89 @@ __global__ void __launch_bounds__(kThreads, 1) la_tc_kernel(const __grid_constan
       src_coord_bilinear(ox, p.scale_w, p.Wi, x0, xp, lx0, lx1);
       const int xa = oc + (oc >= 7 ? 1 : 0);
       const float2 lx0v = make_float2(lx0, lx0), lx1v = make_float2(lx1, lx1);
-      uint32_t r[32];
-      tc_ld32(lane_base + kRsChunk * s0, r);
-      tc_wait_ld_regs(r);
+      // vertical weights of this thread's output rows ry0 .. ry0 + 3 (the
+      // same for every channel step of the tile)
+      float ly0r[4], ly1r[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        int y0, yp;
+        src_coord_bilinear(kRsOutY * (tl.cy0 / kCellsY) + ry0 + i, p.scale_h, p.Hi, y0, yp, ly0r[i], ly1r[i]);
+      }
+      uint32_t pk[16];
+      {
+        uint32_t r[32];
+        tc_ld32(lane_base + kRsChunk * s0, r);
+        tc_wait_ld_regs(r);
+        pack32(r, pk);
+      }
       if (s0 + 1 == s1) {  // last TMEM read of this half is complete
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&out_empty[h]);
       }
-      to_t(region + (step & 1) * kRsTBytes, r);
+      to_t(region + (step & 1) * kRsTBytes, pk);
       for (int sj = s0; sj < s1; ++sj, ++step) {
         const int b = step & 1;
         const uint8_t* sT = region + b * kRsTBytes;
-        uint8_t* sO = region + kRsOffO + b * kRsOSlot;
-        if (leader) bulk_wait_read1();  // the store of two steps ago has read this O buffer
-        named_bar(bar_t, 128);          // T complete (and every thread is past step - 1)
+        named_bar(bar_t, 128);  // T complete (and every thread is past step - 1)
         const bool more = sj + 1 < s1;
-        if (more) tc_ld32(lane_base + kRsChunk * (sj + 1), r);  // lands while this step resamples
         if (worker) {
           // horizontal interpolation of the source rows this thread needs
           // (all loads first), then the vertical one per output row
+          // this thread's 8 channels of output column ox, row 7 * ty (+ R0 + i)
+          T* orow0 = static_cast<T*>(p.rs_out) + tl.b * p.rs_b + (int64_t)(kRsOutY * (tl.cy0 / kCellsY)) * p.rs_h +
+                     (int64_t)ox * p.rs_w + kRsChunk * sj + 8 * cg;
+          // horizontal interpolation of source row yl (lx0 * a + lx1 * b)
+          auto horiz = [&](int yl, float2* hv) {
+            const int pa = yl * 16 + xa, pb = pa + 1;
+            const uint4 va = *reinterpret_cast<const uint4*>(sT + pa * 64 + ((cg ^ ((pa >> 1) & 3)) << 4));
+            const uint4 vb = *reinterpret_cast<const uint4*>(sT + pb * 64 + ((cg ^ ((pb >> 1) & 3)) << 4));
+            const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
+            const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              hv[e] = __ffma2_rn(lx0v, S::unpack2(wa[e]), __fmul2_rn(lx1v, S::unpack2(wb[e])));
+          };
+          // output rows R0 .. R0 + NR - 1 from source rows R0 .. R0 + NR,
+          // two horizontally interpolated rows live at a time
           auto sweep = [&](auto r0c, auto nrc) {
             constexpr int R0 = decltype(r0c)::value, NR = decltype(nrc)::value;
-            uint4 va[NR + 1], vb[NR + 1];
-#pragma unroll
-            for (int i = 0; i <= NR; ++i) {
-              const int pa = (R0 + i) * 16 + xa, pb = pa + 1;
-              va[i] = *reinterpret_cast<const uint4*>(sT + pa * 64 + ((cg ^ ((pa >> 1) & 3)) << 4));
-              vb[i] = *reinterpret_cast<const uint4*>(sT + pb * 64 + ((cg ^ ((pb >> 1) & 3)) << 4));
-            }
-            float2 hr[NR + 1][4];
-#pragma unroll
-            for (int i = 0; i <= NR; ++i) {
-              const uint32_t wa[4] = {va[i].x, va[i].y, va[i].z, va[i].w};
-              const uint32_t wb[4] = {vb[i].x, vb[i].y, vb[i].z, vb[i].w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 a2 = make_float2(S::from_bits((uint16_t)(wa[e] & 0xffffu)), S::from_bits((uint16_t)(wa[e] >> 16)));
-                const float2 b2 = make_float2(S::from_bits((uint16_t)(wb[e] & 0xffffu)), S::from_bits((uint16_t)(wb[e] >> 16)));
-                hr[i][e] = __ffma2_rn(lx0v, a2, __fmul2_rn(lx1v, b2));  // lx0 * a + lx1 * b
-              }
-            }
+            float2 hp[4], hn[4];
+            horiz(R0, hp);
 #pragma unroll
             for (int i = 0; i < NR; ++i) {
-              const int oy = kRsOutY * (tl.cy0 / kCellsY) + R0 + i;
-              int y0, yp;
-              float ly0, ly1;
-              src_coord_bilinear(oy, p.scale_h, p.Hi, y0, yp, ly0, ly1);
-              const float2 ly0v = make_float2(ly0, ly0), ly1v = make_float2(ly1, ly1);
+              horiz(R0 + i + 1, hn);
+              const float2 ly0v = make_float2(ly0r[i], ly0r[i]), ly1v = make_float2(ly1r[i], ly1r[i]);
               uint32_t o[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                const float2 v = __ffma2_rn(ly0v, hr[i][e], __fmul2_rn(ly1v, hr[i + 1][e]));
+                const float2 v = __ffma2_rn(ly0v, hp[e], __fmul2_rn(ly1v, hn[e]));
                 o[e] = S::pack(v.x, v.y);
+                hp[e] = hn[e];
               }
-              *reinterpret_cast<uint4*>(sO + ((R0 + i) * kRsOutX + oc) * 64 + cg * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+              // 16 bytes = 8 channels of one output pixel; a warp writes 8
+              // pixels x 64 contiguous bytes per row
+              *reinterpret_cast<uint4*>(orow0 + (int64_t)(R0 + i) * p.rs_h) = make_uint4(o[0], o[1], o[2], o[3]);
             }
           };
           if (ry0 == 0) sweep(std::integral_constant<int, 0>{}, std::integral_constant<int, 4>{});
           else sweep(std::integral_constant<int, 4>{}, std::integral_constant<int, 3>{});
         }
-        if (more) {
+        if (more) {  // the next step's columns into the other T buffer (read in step - 1, which every
+                     // thread has finished)
+          uint32_t r[32];
+          tc_ld32(lane_base + kRsChunk * (sj + 1), r);
           tc_wait_ld_regs(r);
+          pack32(r, pk);
           if (sj + 2 == s1) {  // last TMEM read of this half is complete
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&out_empty[h]);
           }
-          to_t(region + (b ^ 1) * kRsTBytes, r);  // read in step - 1, which every thread has finished
-        }
-        fence_proxy_async();
-        if (store_warp) {
-          named_bar(bar_o, 128);  // O complete
-          if (leader) {
-            tma_store(&p.omap, sO, kRsChunk * sj, kRsOutX * (tl.cx0 / kCellsX), kRsOutY * (tl.cy0 / kCellsY), tl.b);
-            bulk_commit();
-          }
-        } else {
-          named_arrive(bar_o, 128);
+          to_t(region + (b ^ 1) * kRsTBytes, pk);
         }
       }
     }
-    if (leader) bulk_wait_all();
   }
 
   // ---------------------------------------------------------------- teardown
@@ -915,14 +916,17 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
   if (rc == UPLIFT_LA_OK && a.guide2 != nullptr)
     rc = tc_make_map(&p.gmap2, dt, 2, a.guide2, a.Cg, 2 * a.W, 2 * a.H, a.B, a.g2_w, a.g2_h, a.g2_b, 64, 16, 8);
   if (rc == UPLIFT_LA_OK) rc = tc_make_map(&p.vmap, dt, 2, a.value, a.C, a.W, a.H, a.B, a.v_w, a.v_h, a.v_b, 64, kWinX, 8);
-  if (rc == UPLIFT_LA_OK) {
-    rc = rs ? tc_make_map(&p.omap, dt, 2, a.out, a.C, a.Wo, a.Ho, a.B, a.o_w, a.o_h, a.o_b, kRsChunk, kRsOutX,
-                          kRsOutY, CU_TENSOR_MAP_SWIZZLE_NONE)
-            : tc_make_map(&p.omap, dt, 2, a.out, a.C, 2 * a.W, 2 * a.H, a.B, a.o_w, a.o_h, a.o_b, 64, 16, 2);
-  }
+  if (rc == UPLIFT_LA_OK && !rs)
+    rc = tc_make_map(&p.omap, dt, 2, a.out, a.C, 2 * a.W, 2 * a.H, a.B, a.o_w, a.o_h, a.o_b, 64, 16, 2);
   if (rc != UPLIFT_LA_OK) return rc;
   p.Hi = 2 * a.H;
   p.Wi = 2 * a.W;
+  if (rs) {
+    p.rs_out = a.out;
+    p.rs_b = a.o_b;
+    p.rs_h = a.o_h;
+    p.rs_w = a.o_w;
+  }
   p.scale_h = rs ? (float)p.Hi / (float)a.Ho : 0.f;
   p.scale_w = rs ? (float)p.Wi / (float)a.Wo : 0.f;
   p.weight = a.weight;
