@@ -95,7 +95,7 @@ extern "C" int uplift_la_backward(const void* dout, const int64_t dout_strides[4
   const bool gvec = Cg % ve == 0 && a16(guide) && a.g_b % ve == 0 && a.g_h % ve == 0 && a.g_w % ve == 0;
   // sliding-window dV when the offsets are the reference's table for K; row
   // segments sized so that about 2048 threads per SM are busy
-  bwd::Plan plan{0, 0, 0, W, 1};
+  bwd::Plan plan{0, 0, 0, 0, W, 1};
   {
     // tensor-core dlogit: I = 2, even Cg <= 64, C % 32 == 0 (16-bit storage)
     // or C % 16 == 0 (fp32), 16-byte dout / value rows, aligned guide / dguide
@@ -158,6 +158,26 @@ extern "C" int uplift_la_backward(const void* dout, const int64_t dout_strides[4
     d.B = B; d.C = C; d.H = H; d.W = W; d.I = I; d.K = K; d.dtype = dtype;
     for (int k = 0; k < K; ++k) { d.dy[k] = a.dy[k]; d.dx[k] = a.dx[k]; }
     plan.dv_tc = (dv_env && dv_tc_eligible(d, nullptr)) ? 1 : 0;
+  }
+  if (dtype != UPLIFT_LA_F32) {
+    // tensor-core softmax weights + dlogit: I = 2, 16-bit storage, Cg = 64,
+    // C a multiple of 64 up to 384, offsets within +-2 (ULA_BWD_DL_TC=0
+    // keeps the probs + dlogit kernels, for comparisons)
+    static const bool dl_env = [] {
+      const char* e = getenv("ULA_BWD_DL_TC");
+      return e == nullptr || atoi(e) != 0;
+    }();
+    DlArgs d;
+    d.dout = dout; d.d_b = a.d_b; d.d_h = a.d_h; d.d_w = a.d_w;
+    d.guide = guide; d.g_b = a.g_b; d.g_h = a.g_h; d.g_w = a.g_w;
+    d.value = value; d.v_b = a.v_b; d.v_h = a.v_h; d.v_w = a.v_w;
+    d.weight = weight; d.bias = bias; d.probs = probs;
+    d.dguide = dguide; d.dg_b = a.dg_b; d.dg_h = a.dg_h; d.dg_w = a.dg_w;
+    d.dweight = dweight; d.dbias = dbias;
+    d.B = B; d.Cg = Cg; d.C = C; d.H = H; d.W = W; d.I = I; d.K = K; d.dtype = dtype;
+    d.conv_res = a.conv_res; d.hardmax = a.hardmax;
+    for (int k = 0; k < K; ++k) { d.dy[k] = a.dy[k]; d.dx[k] = a.dx[k]; }
+    plan.dl_tc = (dl_env && dl_tc_eligible(d, nullptr)) ? 1 : 0;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {

@@ -920,6 +920,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, 2) dlogit_mma_kernel(const Arg
 struct Plan {
   int mma_pn;    // 1 or 2: tensor-core dlogit (dlogit_mma_kernel<PN>); 0: CUDA-core dlogit
   int dv_tc;     // 1: tensor-core dV (la_bwd_dv.cu)
+  int dl_tc;     // 1: tensor-core softmax weights + dlogit (la_bwd_dl.cu) instead of probs + dlogit kernels
   int window;    // 1: sliding-window dV (reference offset table); 0: general dV kernel
   int seg_len;   // value columns per window thread
   int nseg;
@@ -941,10 +942,28 @@ int launch_cv(const Args& a, const Plan& plan, cudaStream_t stream) {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(dlogit_kernel<T, K, CPT, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_d);
   if (e != cudaSuccess) return fail(UPLIFT_LA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-  const int64_t pblocks = std::min<int64_t>((npix + kThreads - 1) / kThreads, (int64_t)sms * 16);
-  probs_kernel<T, K, GV><<<(unsigned)pblocks, kThreads, smem_p, stream>>>(a);
   bool dlogit_done = false;
-  {
+  if (plan.dl_tc) {
+    DlArgs d;
+    d.dout = a.dout; d.d_b = a.d_b; d.d_h = a.d_h; d.d_w = a.d_w;
+    d.guide = a.guide; d.g_b = a.g_b; d.g_h = a.g_h; d.g_w = a.g_w;
+    d.value = a.value; d.v_b = a.v_b; d.v_h = a.v_h; d.v_w = a.v_w;
+    d.weight = a.weight; d.bias = a.bias;
+    d.probs = a.dvalue != nullptr ? a.probs : nullptr;
+    d.dguide = a.dguide; d.dg_b = a.dg_b; d.dg_h = a.dg_h; d.dg_w = a.dg_w;
+    d.dweight = a.dweight; d.dbias = a.dbias;
+    d.B = a.B; d.Cg = a.Cg; d.C = a.C; d.H = a.H; d.W = a.W; d.I = a.I; d.K = K;
+    d.dtype = std::is_same<T, __nv_bfloat16>::value ? UPLIFT_LA_BF16 : UPLIFT_LA_F16;
+    d.conv_res = a.conv_res; d.hardmax = a.hardmax;
+    for (int k = 0; k < K; ++k) { d.dy[k] = a.dy[k]; d.dx[k] = a.dx[k]; }
+    const int rc = dl_tc_launch(d, stream);
+    if (rc != UPLIFT_LA_OK) return rc;
+    dlogit_done = true;
+  } else {
+    const int64_t pblocks = std::min<int64_t>((npix + kThreads - 1) / kThreads, (int64_t)sms * 16);
+    probs_kernel<T, K, GV><<<(unsigned)pblocks, kThreads, smem_p, stream>>>(a);
+  }
+  if (!dlogit_done) {
     if (plan.mma_pn > 0 && (a.dguide != nullptr || a.dweight != nullptr || a.dbias != nullptr)) {
       auto kern = plan.mma_pn == 1 ? dlogit_mma_kernel<T, K, 1> : dlogit_mma_kernel<T, K, 2>;
       const size_t smem_m =

@@ -74,6 +74,23 @@ bool dv_tc_eligible(const DvArgs& a, const char** why);
 int dv_tc_launch(const DvArgs& a, cudaStream_t stream);
 int dv_device_status(bool clear);
 
+// Tensor-core dlogit of the backward (la_bwd_dl.cu): softmax weights (into
+// the workspace), dguide and dW / db (accumulated) for 16-bit storage.
+struct DlArgs {
+  const void* dout;   int64_t d_b, d_h, d_w;
+  const void* guide;  int64_t g_b, g_h, g_w;
+  const void* value;  int64_t v_b, v_h, v_w;
+  const float* weight; const float* bias;
+  float* probs;        // [B][I*H][I*W][K] or null
+  void* dguide;       int64_t dg_b, dg_h, dg_w;  // or null
+  float* dweight; float* dbias;                   // or null
+  int B, Cg, C, H, W, I, K, dtype, conv_res, hardmax;
+  int8_t dy[25], dx[25];
+};
+bool dl_tc_eligible(const DlArgs& a, const char** why);
+int dl_tc_launch(const DlArgs& a, cudaStream_t stream);
+int dl_device_status(bool clear);
+
 // Record an error message for uplift_la_last_error().
 int fail(int code, const char* fmt, ...);
 

@@ -172,6 +172,29 @@ constexpr uint32_t kLayoutNone = 0, kLayoutSw128 = 2;
 __host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_fmt, uint32_t b_mn_major, uint32_t m, uint32_t n) {
   return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (b_mn_major << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
+// The same with the A operand's major-ness too (bit 15: A MN-major).
+__host__ __device__ constexpr uint32_t idesc_f16_ab(uint32_t ab_fmt, uint32_t a_mn_major, uint32_t b_mn_major,
+                                                    uint32_t m, uint32_t n) {
+  return idesc_f16(ab_fmt, b_mn_major, m, n) | (a_mn_major << 15);
+}
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+// tcgen05.wait::ld naming the 16 registers of an earlier tc_ld16.
+__device__ __forceinline__ void tc_wait_ld_regs16(uint32_t* r) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+        "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+      :
+      : "memory");
+}
 
 }  // namespace tc
 }  // namespace ula

@@ -436,8 +436,9 @@ int uplift_la_device_status(int clear) {
   const int a = ula::tc_device_status(clear != 0);
   const int b = ula::tcw_device_status(clear != 0);
   const int c = ula::dv_device_status(clear != 0);
-  if (a < 0 || b < 0 || c < 0) return -1;
-  return a != 0 ? a : (b != 0 ? b : c);
+  const int d = ula::dl_device_status(clear != 0);
+  if (a < 0 || b < 0 || c < 0 || d < 0) return -1;
+  return a != 0 ? a : (b != 0 ? b : (c != 0 ? c : d));
 }
 
 int uplift_la_set_host_status_word(unsigned int* word) {
