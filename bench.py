@@ -600,11 +600,14 @@ def run_backward(dev, stream, peak, images, reps=5):
     """Device time of the attender backward (training; uplift_la_backward:
     dguide, dvalue, dweight, dbias) on the four levels of the chain above,
     bf16, `images` per GPU, random-init LocalAttender(64, 17), N(0,1) guide /
-    value / output gradient.  Eager calls (each allocates its outputs and
-    workspace from torch's cache), median of `reps` after 2 warm calls.
-    Algorithmic bytes per output pixel: dout + guide read, dguide written
-    ((C + 2 Cg) * 2), the fp32 softmax workspace written once and read twice
-    (12 K), value read and dvalue written once per value pixel (2 C * 2 / 4)."""
+    value / output gradient.  Each level's call (output allocation, the
+    zeroing of dW / db and every kernel) is captured in a CUDA graph and
+    replayed `reps` times with an L2 flush before each replay (median);
+    `ms_eager` is one eager call from the host, median of `reps` (it adds
+    the Python wrapper's launch latency).  Algorithmic bytes per output
+    pixel: dout + guide read, dguide written ((C + 2 Cg) * 2), the fp32
+    softmax workspace written once and read twice (12 K), value read and
+    dvalue written once per value pixel (2 C * 2 / 4)."""
     from uplift_b200 import ops
     from uplift_b200.attender import LocalAttender, neighbourhood
 
@@ -616,34 +619,60 @@ def run_backward(dev, stream, peak, images, reps=5):
     g = torch.Generator().manual_seed(0)
     cl = torch.channels_last
     bpp = (C + 2 * CG) * ELEM + 12 * K_NBR + 2 * C * ELEM / 4
-    levels, tot_ms, tot_px = [], 0.0, 0
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    cap = torch.cuda.Stream(dev)  # graphs are captured off the default stream
+    levels, tot_ms, tot_px, tot_eager = [], 0.0, 0, 0.0
+
+    def timed_once(fn):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record(stream)
+        fn()
+        ev[1].record(stream)
+        ev[1].synchronize()
+        return ev[0].elapsed_time(ev[1])
+
     with torch.cuda.stream(stream):
         for co, fo in LEVELS:
             guide = torch.randn(images, CG, fo, fo, generator=g).to(torch.bfloat16).to(dev).contiguous(memory_format=cl)
             value = torch.randn(images, C, co, co, generator=g).to(torch.bfloat16).to(dev).contiguous(memory_format=cl)
             dout = torch.randn(images, C, fo, fo, generator=g).to(torch.bfloat16).to(dev).contiguous(memory_format=cl)
+
+            def call():
+                return ops.local_attender_backward_raw(dout, guide, value, w, b, offsets, pn)
+
             for _ in range(2):
-                ops.local_attender_backward_raw(dout, guide, value, w, b, offsets, pn)
+                call()
+            eager = []
+            for _ in range(reps):
+                flush.zero_()
+                eager.append(timed_once(call))
+            graph = torch.cuda.CUDAGraph()
+            cap.wait_stream(stream)
+            with torch.cuda.graph(graph, stream=cap):
+                outs = call()
+            stream.wait_stream(cap)
+            graph.replay()
             times = []
             for _ in range(reps):
-                ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-                ev[0].record(stream)
-                ops.local_attender_backward_raw(dout, guide, value, w, b, offsets, pn)
-                ev[1].record(stream)
-                ev[1].synchronize()
-                times.append(ev[0].elapsed_time(ev[1]))
+                flush.zero_()
+                times.append(timed_once(graph.replay))
+            del graph, outs
             ms = statistics.median(times)
             px = images * fo * fo
             tot_ms += ms
+            tot_eager += statistics.median(eager)
             tot_px += px
-            levels.append({"level": f"{co}^2->{fo}^2", "ms": round(ms, 4), "Mpix_s": round(px / ms / 1e3, 1),
-                           "GB_s": round(px * bpp / ms / 1e6, 1)})
+            levels.append({"level": f"{co}^2->{fo}^2", "ms": round(ms, 4), "ms_eager": round(statistics.median(eager), 4),
+                           "Mpix_s": round(px / ms / 1e3, 1), "GB_s": round(px * bpp / ms / 1e6, 1)})
             del guide, value, dout
-    return {"levels": levels, "ms_chain": round(tot_ms, 4), "Mpix_s_chain": round(tot_px / tot_ms / 1e3, 1),
+    del flush
+    return {"levels": levels, "ms_chain": round(tot_ms, 4), "ms_chain_eager": round(tot_eager, 4),
+            "Mpix_s_chain": round(tot_px / tot_ms / 1e3, 1),
             "frac_of_peak_chain": round(tot_px * bpp / tot_ms / 1e6 / peak, 4), "algo_bytes_per_pixel": bpp,
-            "launches_per_level": 3, "dtype": "bf16", "images": images,
-            "note": "probs / dlogit / dvalue kernels; eager calls, median of 5; "
-                    "frac against the measured HBM copy peak"}
+            "launches_per_level": 2, "dtype": "bf16", "images": images,
+            "note": "tensor-core dlogit + tensor-core dV kernels (and the zeroing of dW / db); CUDA-graph "
+                    "replay of each level's call, L2 flushed before each, median of 5; frac against the measured "
+                    "HBM copy peak"}
 
 
 def run_e2e(la, host, dev, stream, world, args, mpix_step):

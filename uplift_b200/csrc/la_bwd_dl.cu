@@ -20,15 +20,21 @@
 // written to the fp32 workspace the tensor-core dV (la_bwd_dv.cu) reads.
 // Reference: autograd through LocalAttender.forward, uplift/uplift.py:801-847.
 //
-// Roles (448 threads, one CTA per SM, persistent over tiles): warp 0 TMA
-// producer (guide tile; dout and value window in 64-channel chunks through a
-// 3-stage ring); warp 1 TMEM owner + MMA issuer (logits and dP of tile n+1
-// before dguide and dW of tile n); warps 2-9 two compute warpgroups (even /
-// odd tiles; a thread per pixel); warps 10-13 dguide epilogue (TMEM ->
-// storage type -> swizzled staging -> TMA store) and, at the end, the dW /
-// db atomics.  Every mbarrier wait is bounded; on expiry the CTA records the
-// role in this kernel's status word (and the registered host word), drains
-// and exits.
+// Roles (480 threads, one CTA per SM, persistent over tiles): warp 0 TMA
+// producer (guide tile into one of four slots -- a tile's guide is held from
+// its load to its dW, and four slots let the next tiles' guides load while
+// that runs; dout and value window in 64-channel chunks through a 3-stage
+// ring); warp 1 TMEM owner + front MMA issuer (logits and dP of every tile,
+// up to three tiles ahead of the compute warps: three TMEM slots); warp 14
+// back MMA issuer (dW and dguide of each tile as its dl arrives, so that
+// they never hold up the next tiles' dP); warps 2-9 two compute warpgroups
+// (even / odd tiles; a thread per pixel); warps 10-13 dguide epilogue (TMEM
+// -> storage type -> swizzled staging -> TMA store) and, at the end, the
+// dW / db atomics.  Every mbarrier wait is bounded; on expiry the CTA
+// records the role in this kernel's status word (and the registered host
+// word), drains and exits.  The wait's completed-phase test is inlined: a
+// call into the bounded slow path costs a single-thread issuer hundreds of
+// cycles, and the issuers pass about ten waits per tile.
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -59,7 +65,7 @@ constexpr int kWinX = 12, kWin = 96;           // value window 8 x 12 (pn <= 2)
 constexpr int kChunk = 64;
 constexpr int kMaxC = 384;
 constexpr int kLogN = 32;
-constexpr int kThreads = 448;
+constexpr int kThreads = 480;
 constexpr int kTmemCols = 512;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 
@@ -67,30 +73,34 @@ constexpr int kGBytes = kM * 128;              // 16 KB: 128 px x 64 ch (guide t
 constexpr int kVBytes = kWin * 128;            // 12 KB: 96 px x 64 ch
 constexpr int kStageBytes = kGBytes + kVBytes; // 28 KB: dout box + value box
 constexpr int kStages = 3;
+constexpr int kSlots = 3;                      // logits / dP TMEM slots
+constexpr int kGSlots = 4;                     // guide slots: a tile's guide is held from its load to its dW
+constexpr int kConstBytes = 16 * 128;          // 2 KB: the ones channel for one 16-pixel K step
 constexpr int kWBytes = kLogN * 128;           // 4 KB: 32 logits x 64 ch
 constexpr int kDlBytes = kM * 128;             // 16 KB: per pixel [dl_hi x 32 | dl_lo x 32]
 constexpr int kWarpStage = 32 * 128;           // 4 KB
 
-constexpr int kOffG = 0;                              // 2 guide slots
-constexpr int kOffConst = kOffG + 2 * kGBytes;        // the ones channel (db) beside the guide
-constexpr int kOffRing = kOffConst + kGBytes;
+constexpr int kOffG = 0;                                  // kGSlots guide slots
+constexpr int kOffConst = kOffG + kGSlots * kGBytes;      // the ones channel (db) beside the guide
+constexpr int kOffRing = kOffConst + kConstBytes;
 constexpr int kOffW = kOffRing + kStages * kStageBytes;   // W_hi, W_lo
 constexpr int kOffWg = kOffW + 2 * kWBytes;               // dguide B: [W_hi | W_hi], [W_lo | I]
 constexpr int kWgBytes = 64 * 128;                        // 64 guide channels x 64
 constexpr int kOffDl = kOffWg + 2 * kWgBytes;             // 2 dl buffers
 constexpr int kOffStage = kOffDl + 2 * kDlBytes;
-constexpr int kOffBias = kOffStage + 4 * 2 * kWarpStage;
+constexpr int kOffBias = kOffStage + 4 * kWarpStage;
 constexpr int kOffBar = kOffBias + kLogN * 4;
-constexpr int kNumBars = 2 + 2 + kStages + kStages + 2 + 2 + 2 + 2 + 2 + 2 + 2 + 2 + 1 + 1;
+constexpr int kNumBars = 2 * kGSlots + 4 * kSlots + 2 * kStages + 2 + 2 + 1 + 1 + 1 + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 16 + 1024;
 static_assert(kSmemBytes <= 232448, "shared memory");
 
 // TMEM columns
-constexpr int kColLog = 0;     // 2 x 32
-constexpr int kColDp = 64;     // 2 x 96
-constexpr int kColDw = 256;    // 64: rows = guide channels (0-63) and the ones channel (64)
-constexpr int kColDg = 320;    // 2 x 64
+constexpr int kColLog = 0;     // kSlots x 32
+constexpr int kColDp = 96;     // kSlots x 96
+constexpr int kColDw = 384;    // 64: rows = guide channels (0-63) and the ones channel (64)
+constexpr int kColDg = 448;    // 64 (one slot: the epilogue releases it right after its load)
+static_assert(kColDp == kSlots * kLogN && kColDw == kColDp + kSlots * kWin && kColDg + 64 == kTmemCols, "TMEM");
 
 struct Params {
   CUtensorMap gmap;   // guide  [B, 2H, 2W, 64]  box {64, 16, 8, 1}
@@ -113,6 +123,7 @@ struct Params {
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, unsigned where,
                                           const WaitLimit& limit) {
+  if (mbar_try(b, parity)) return true;  // completed phase: no call into the bounded slow path
   return mbar_wait_status(b, parity, abort_flag, where, limit, &g_dl_status);
 }
 
@@ -168,18 +179,18 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
   float* sBias = reinterpret_cast<float*>(smem + kOffBias);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* g_full = bars;
-  uint64_t* g_empty = g_full + 2;
-  uint64_t* r_full = g_empty + 2;
+  uint64_t* g_empty = g_full + kGSlots;
+  uint64_t* r_full = g_empty + kGSlots;
   uint64_t* r_empty = r_full + kStages;
   uint64_t* log_full = r_empty + kStages;
-  uint64_t* log_empty = log_full + 2;
-  uint64_t* dp_full = log_empty + 2;
-  uint64_t* dp_empty = dp_full + 2;
-  uint64_t* dl_full = dp_empty + 2;
+  uint64_t* log_empty = log_full + kSlots;
+  uint64_t* dp_full = log_empty + kSlots;
+  uint64_t* dp_empty = dp_full + kSlots;
+  uint64_t* dl_full = dp_empty + kSlots;
   uint64_t* dl_empty = dl_full + 2;
   uint64_t* dg_full = dl_empty + 2;
-  uint64_t* dg_empty = dg_full + 2;
-  uint64_t* dw_done = dg_empty + 2;
+  uint64_t* dg_empty = dg_full + 1;
+  uint64_t* dw_done = dg_empty + 1;
   uint64_t* drain = dw_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
@@ -187,24 +198,28 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kGSlots; ++i) {
       mbar_init(&g_full[i], 1);
       mbar_init(&g_empty[i], 1);    // dW MMA of the tile done
+    }
+    for (int i = 0; i < kSlots; ++i) {
       mbar_init(&log_full[i], 1);
       mbar_init(&log_empty[i], 4);  // 4 compute warps
       mbar_init(&dp_full[i], 1);
       mbar_init(&dp_empty[i], 4);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&dl_full[i], 4);
       mbar_init(&dl_empty[i], 1);
-      mbar_init(&dg_full[i], 1);
-      mbar_init(&dg_empty[i], 4);   // 4 epilogue warps
     }
+    mbar_init(dg_full, 1);
+    mbar_init(dg_empty, 4);         // 4 epilogue warps
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&r_full[i], 1);
       mbar_init(&r_empty[i], 1);
     }
     mbar_init(dw_done, 1);
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);
     abort_flag[0] = 0;
     abort_flag[1] = 0;  // stays 0: the flag of waits that must not be aborted
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -230,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
     *reinterpret_cast<uint16_t*>(sWg + kWgBytes + sw128(c, n + 32)) =
         (n < p.res_k && n == c) ? S::bits(1.f) : (uint16_t)0;
   }
-  for (int idx = tid; idx < kM * 64; idx += kThreads) {
+  for (int idx = tid; idx < 16 * 64; idx += kThreads) {
     const int px = idx >> 6, c = idx & 63;
     *reinterpret_cast<uint16_t*>(sConst + sw128(px, c)) = (c == 0) ? S::bits(1.f) : (uint16_t)0;
   }
@@ -255,8 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
       uint32_t rc = 0;
       for (int n = 0; n < local_tiles && ok; ++n) {
         const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
-        const int s = n & 1;
-        ok = mbar_wait(&g_empty[s], ((n >> 1) & 1) ^ 1, abort_flag, 1, tmo);
+        const int s = n % kGSlots;
+        ok = mbar_wait(&g_empty[s], ((n / kGSlots) & 1) ^ 1, abort_flag, 1, tmo);
         if (!ok) break;
         mbar_expect_tx(&g_full[s], kGBytes);
         tma_load(sG + s * kGBytes, &p.gmap, &g_full[s], 0, 2 * tl.cx0, 2 * tl.cy0, tl.b);
@@ -275,8 +290,11 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
         while (gtimer() - t0 < 200000ull) {}
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == 14) {
+    // ------------------------------------------------------------ MMA issuers
+    // warp 1: logits and dP (front) of every tile, as far ahead as the TMEM
+    // slots and the loads allow; warp 14: dW and dguide (back), as each
+    // tile's dl arrives.  Each commits only its own MMAs.
     if (lane == 0) {
       constexpr uint32_t kIdLog = idesc_f16(S::kFmt, 0, kM, kLogN);
       constexpr uint32_t kIdDp = idesc_f16(S::kFmt, 0, kM, kWin);
@@ -286,12 +304,12 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
       uint32_t rc = 0;
       bool ok = true, first_dw = true;
       auto front = [&](int n) -> bool {  // logits and dP of tile n
-        const int s = n & 1;
-        const uint32_t ph = (n >> 1) & 1;
-        if (!mbar_wait(&g_full[s], ph, abort_flag, 2, tmo)) return false;
+        const int s = n % kSlots, sg = n % kGSlots;
+        const uint32_t ph = (n / kSlots) & 1;
+        if (!mbar_wait(&g_full[sg], (n / kGSlots) & 1, abort_flag, 2, tmo)) return false;
         if (!mbar_wait(&log_empty[s], ph ^ 1, abort_flag, 2, tmo)) return false;
         tc_fence_after();
-        const uint32_t aG = su32(sG + s * kGBytes);
+        const uint32_t aG = su32(sG + sg * kGBytes);
 #pragma unroll
         for (int src = 0; src < 2; ++src)
 #pragma unroll
@@ -316,19 +334,19 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
         return true;
       };
       auto back = [&](int n) -> bool {  // dW and dguide of tile n
-        const int s = n & 1;
-        const uint32_t ph = (n >> 1) & 1;
-        if (!mbar_wait(&dl_full[s], ph, abort_flag, 2, tmo)) return false;
-        if (!mbar_wait(&dg_empty[s], ph ^ 1, abort_flag, 2, tmo)) return false;
+        const int sg = n % kGSlots, s = n & 1;
+        if (!mbar_wait(&dl_full[s], (n >> 1) & 1, abort_flag, 2, tmo)) return false;
+        if (!mbar_wait(dg_empty, (n & 1) ^ 1, abort_flag, 2, tmo)) return false;
         tc_fence_after();
-        const uint32_t aG = su32(sG + s * kGBytes);
+        const uint32_t aG = su32(sG + sg * kGBytes);
         const uint32_t aDl = su32(sDl + s * kDlBytes);
         // dW^T[128 x 64] += [G | 1]^T . [dl_hi | dl_lo]: A MN-major (M =
-        // channels in two 64-wide blocks: the guide tile, then the ones
-        // tile), B MN-major (N = the 64 dl columns), K = the 128 pixels
+        // channels in two 64-wide blocks: the guide tile's 16 pixels of the
+        // K step, then the 16 rows of the ones tile, the same for every
+        // step), B MN-major (N = the 64 dl columns), K = the 128 pixels
 #pragma unroll
         for (int ks = 0; ks < kM / 16; ++ks)
-          tc_mma(tmem + kColDw, mdesc(aG + 2048 * ks, aConst - aG, 1024, kLayoutSw128),
+          tc_mma(tmem + kColDw, mdesc(aG + 2048 * ks, aConst - (aG + 2048 * ks), 1024, kLayoutSw128),
                  mdesc(aDl + 2048 * ks, kDlBytes, 1024, kLayoutSw128), kIdDw, (first_dw && ks == 0) ? 0u : 1u);
         first_dw = false;
         // dguide[128 x 64]: both operands K-major in 16-column slices; dl
@@ -339,27 +357,25 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
         constexpr int kDgB[10] = {0, 1, 2, 3, 4, 5, 6, 7, 6, 7};
 #pragma unroll
         for (int m = 0; m < 10; ++m)
-          tc_mma(tmem + kColDg + 64 * s, mdesc(aDl + 32 * kDgA[m], 16, 1024, kLayoutSw128),
+          tc_mma(tmem + kColDg, mdesc(aDl + 32 * kDgA[m], 16, 1024, kLayoutSw128),
                  mdesc(aWg + (kDgB[m] >> 2) * kWgBytes + 32 * (kDgB[m] & 3), 16, 1024, kLayoutSw128), kIdDg,
                  m > 0);
         tc_commit(&dl_empty[s]);
-        tc_commit(&g_empty[s]);
-        tc_commit(&dg_full[s]);
+        tc_commit(&g_empty[sg]);
+        tc_commit(dg_full);
         return true;
       };
-      if (local_tiles > 0) ok = front(0);
-      for (int n = 0; n < local_tiles && ok; ++n) {
-        if (n + 1 < local_tiles) {
-          ok = front(n + 1);
-          if (!ok) break;
-        }
-        ok = back(n);
+      if (warp == 1) {
+        for (int n = 0; n < local_tiles && ok; ++n) ok = front(n);
+      } else {
+        for (int n = 0; n < local_tiles && ok; ++n) ok = back(n);
+        tc_commit(dw_done);  // every dW MMA is complete
       }
-      tc_commit(dw_done);  // every MMA issued so far, the last dW among them, is complete
-      // all issued MMAs complete before TMEM can be released (this wait
-      // ignores the abort flag: it must not be cut short by another role)
+      // all issued MMAs complete before TMEM can be released (the drain
+      // barrier takes both issuers' commits; the wait ignores the abort
+      // flag: it must not be cut short by another role)
       tc_commit(drain);
-      mbar_wait(drain, 0, abort_flag + 1, 2, tmo);
+      if (warp == 1) mbar_wait(drain, 0, abort_flag + 1, 2, tmo);
     }
   } else if (warp < 10) {
     // ------------------------------------------------------------ compute
@@ -374,8 +390,8 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
     for (int n = wg; n < local_tiles; n += 2) {
       const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
-      const int s = n & 1;
-      const uint32_t ph = (n >> 1) & 1;
+      const int s = n % kSlots, sd = n & 1, sg = n % kGSlots;
+      const uint32_t ph = (n / kSlots) & 1;
       if (!mbar_wait(&log_full[s], ph, abort_flag, 3, tmo)) break;
       tc_fence_after();
       uint32_t r[32];
@@ -384,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&log_empty[s]);
-      if (!mbar_wait(&g_full[s], ph, abort_flag, 3, tmo)) break;
+      if (!mbar_wait(&g_full[sg], (n / kGSlots) & 1, abort_flag, 3, tmo)) break;
       const int oy = 2 * tl.cy0 + py, ox = 2 * tl.cx0 + px;
       const bool inside = oy < 2 * p.H && ox < 2 * p.W;
       float pk[K];
@@ -393,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
 #pragma unroll
         for (int k = 0; k < K; ++k) lg[k] = __uint_as_float(r[k]) + sBias[k];
         if (p.res_k > 0) {  // residual_auto: + guide[k] for k < min(K, Cg)
-          const uint8_t* grow = sG + s * kGBytes + i * 128;
+          const uint8_t* grow = sG + sg * kGBytes + i * 128;
 #pragma unroll
           for (int c8 = 0; c8 < (K + 7) / 8; ++c8) {
             const uint4 v = *reinterpret_cast<const uint4*>(grow + ((c8 ^ (i & 7)) << 4));
@@ -475,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
       float dot = 0.f;
 #pragma unroll
       for (int k = 0; k < K; ++k) dot = fmaf(pk[k], dp[k], dot);
-      if (!mbar_wait(&dl_empty[s], ph ^ 1, abort_flag, 3, tmo)) break;
+      if (!mbar_wait(&dl_empty[sd], ((n >> 1) & 1) ^ 1, abort_flag, 3, tmo)) break;
       uint32_t hi[16], lo[16];
 #pragma unroll
       for (int k2 = 0; k2 < 16; ++k2) {
@@ -487,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
         const float h0 = S::from_bits((uint16_t)(hi[k2] & 0xffffu)), h1 = S::from_bits((uint16_t)(hi[k2] >> 16));
         lo[k2] = S::pack(d0 - h0, d1 - h1);
       }
-      uint8_t* drow = sDl + s * kDlBytes + i * 128;
+      uint8_t* drow = sDl + sd * kDlBytes + i * 128;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         *reinterpret_cast<uint4*>(drow + ((c ^ (i & 7)) << 4)) =
@@ -497,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
       }
       fence_proxy_async();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&dl_full[s]);
+      if (lane == 0) mbar_arrive(&dl_full[sd]);
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -505,26 +521,24 @@ __global__ void __launch_bounds__(kThreads, 1) la_dl_tc_kernel(const __grid_cons
     // the tile and stores them through its own two staging buffers
     const int q = warp & 3;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-    uint8_t* bufs = sStage + (warp - 10) * 2 * kWarpStage;
+    uint8_t* buf = sStage + (warp - 10) * kWarpStage;
     bool ok = true;
     for (int n = 0; n < local_tiles; ++n) {
       const TileXY tl = tile_of(p, blockIdx.x + n * gridDim.x);
-      const int s = n & 1;
-      if (!mbar_wait(&dg_full[s], (n >> 1) & 1, abort_flag, 4, tmo)) {
+      if (!mbar_wait(dg_full, n & 1, abort_flag, 4, tmo)) {
         ok = false;
         break;
       }
       tc_fence_after();
       uint32_t r[64];
-      tc_ld32(lane_base + kColDg + 64 * s, r);
-      tc_ld32(lane_base + kColDg + 64 * s + 32, r + 32);
+      tc_ld32(lane_base + kColDg, r);
+      tc_ld32(lane_base + kColDg + 32, r + 32);
       tc_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&dg_empty[s]);
+      if (lane == 0) mbar_arrive(dg_empty);
       if (!p.write_dguide) continue;
-      uint8_t* buf = bufs + (n & 1) * kWarpStage;
-      if (lane == 0) bulk_wait_read1();  // the store issued two tiles ago has read `buf`
+      if (lane == 0) bulk_wait_read0();  // the store of the previous tile has read `buf`
       __syncwarp();
       uint8_t* rowp = buf + lane * 128;
 #pragma unroll

@@ -113,6 +113,7 @@ struct Params {
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, unsigned where,
                                           const WaitLimit& limit) {
+  if (mbar_try(b, parity)) return true;  // completed phase: no call into the bounded slow path
   return mbar_wait_status(b, parity, abort_flag, where, limit, &g_tcw_status);
 }
 
