@@ -23,7 +23,9 @@
 //
 // Roles (320 threads, one CTA per SM, persistent over tiles): warp 0 TMA
 // producer of the dout ring; warp 1 TMEM owner + MMA issuer; warps 2-5 build
-// Pt (double-buffered); warps 6-9 epilogue (TMEM -> storage type -> swizzled
+// Pt (double-buffered; each thread owns a column, clears its own earlier
+// entries instead of a zero pass, and loads the next cell row's weights
+// while scattering the current one); warps 6-9 epilogue (TMEM -> storage type -> swizzled
 // staging -> TMA store of the warp's 2 value rows).  Every mbarrier wait is
 // bounded; on expiry the CTA records the role in this kernel's status word
 // (and the registered host word), drains and exits.
@@ -242,66 +244,106 @@ __global__ void __launch_bounds__(kThreads, 1) la_dv_tc_kernel(const __grid_cons
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------ Pt builders
-    // thread i < 80 owns output pixel i of the cell row (2 rows x 40
-    // columns): it scatters that pixel's softmax weights into column i of Pt;
-    // all 128 threads zero the buffer first.  One thread waits on the
-    // buffer's barrier and shares the outcome, so all take the same path.
+    // thread t < 80 owns output pixel t of the cell row (2 rows x 40
+    // columns), i.e. column t of Pt: it scatters that pixel's softmax
+    // weights into its column, and before that clears the entries it set
+    // in the same buffer two cell rows earlier (both buffers are zeroed
+    // once at the start), so no thread waits for another.  The weights of
+    // the next cell row are loaded while the current one is scattered.
     const int t = tid - 64;
-    uint32_t gc = 0;
-    bool ok = true;
-    for (int n = 0; n < local_tiles && ok; ++n) {
-      const Tile tl = tile_of(p, blockIdx.x + n * gridDim.x);
-      for (int cy = tl.r0; cy < tl.r1; ++cy, ++gc) {
-        const int pb = gc & 1;
-        if (t == 0) *go = mbar_wait(&pt_empty[pb], ((gc >> 1) & 1) ^ 1, abort_flag, 3, tmo) ? 1 : 0;
-        named_bar(1, 128);
-        if (*go == 0) {
-          ok = false;
-          break;
+    const int py = t / (2 * kRegX), px = t - py * (2 * kRegX);
+    for (int i = t; i < 2 * kPtBytes / 16; i += 128) reinterpret_cast<uint4*>(sPt)[i] = make_uint4(0, 0, 0, 0);
+    named_bar(1, 128);
+    // the stage after (n, cy): next cell row of the tile, else the next tile's first
+    auto next_stage = [&](int& n, int& cy, Tile& tl) {
+      if (++cy >= tl.r1) {
+        if (++n < local_tiles) {
+          tl = tile_of(p, blockIdx.x + n * gridDim.x);
+          cy = tl.r0;
         }
-        uint8_t* buf = sPt + pb * kPtBytes;
-        for (int i = t; i < kPtBytes / 16; i += 128) reinterpret_cast<uint4*>(buf)[i] = make_uint4(0, 0, 0, 0);
-        named_bar(1, 128);
-        if (t < kKc) {
-          const int py = t / (2 * kRegX), px = t - py * (2 * kRegX);
-          const int oy = 2 * cy + py, ox = 2 * (tl.vx0 - kPn) + px;
-          if (ox >= 0 && ox < 2 * p.W) {
-            const int cx = ox >> 1;
-            const float* pr = p.probs + (((int64_t)tl.b * 2 * p.H + oy) * (2 * p.W) + ox) * K;
-            float pk[K];
-            int nk[K];
-            bool border = false;
+      }
+    };
+    auto load_probs = [&](int n, int cy, const Tile& tl, float* dst) {
+      const int oy = 2 * cy + py, ox = 2 * (tl.vx0 - kPn) + px;
+      if (n < local_tiles && t < kKc && ox >= 0 && ox < 2 * p.W) {
+        const float* pr = p.probs + (((int64_t)tl.b * 2 * p.H + oy) * (2 * p.W) + ox) * K;
 #pragma unroll
-            for (int k = 0; k < K; ++k) {
-              pk[k] = __ldg(pr + k);
-              const int yy = cy + p.dy[k], xx = cx + p.dx[k];
-              border |= yy < 0 || yy >= p.H || xx < 0 || xx >= p.W;
-              const int ny = min(max(yy, 0), p.H - 1) - tl.vy0, nx = min(max(xx, 0), p.W - 1) - tl.vx0;
-              nk[k] = (ny >= 0 && ny < kTy && nx >= 0 && nx < kTx) ? ny * kTx + nx : -1;
-            }
-            if (border) {  // offsets that clamp onto the same value pixel are summed in fp32
+        for (int k = 0; k < K; ++k) dst[k] = __ldg(pr + k);
+      }
+    };
+    int8_t prev0[K], prev1[K];  // the entries this thread set in buffer 0 / 1
 #pragma unroll
-              for (int k = 1; k < K; ++k) {
+    for (int k = 0; k < K; ++k) prev0[k] = prev1[k] = -1;
+    float pk[K], pn[K];
 #pragma unroll
-                for (int j = 0; j < k; ++j) {
-                  if (nk[k] >= 0 && nk[j] == nk[k]) {
-                    pk[j] += pk[k];
-                    nk[k] = -1;
-                  }
+    for (int k = 0; k < K; ++k) pk[k] = pn[k] = 0.f;
+    int n = 0, cy = 0;
+    Tile tl{};
+    if (local_tiles > 0) {
+      tl = tile_of(p, blockIdx.x);
+      cy = tl.r0;
+      load_probs(n, cy, tl, pn);
+    }
+    uint32_t gc = 0;
+    while (n < local_tiles) {
+      const int pb = gc & 1;
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(&pt_empty[pb], ((gc >> 1) & 1) ^ 1, abort_flag, 3, tmo) ? 1 : 0;
+      if (__shfl_sync(0xffffffffu, ok, 0) == 0) break;
+#pragma unroll
+      for (int k = 0; k < K; ++k) pk[k] = pn[k];
+      const int ccy = cy;
+      const Tile ctl = tl;
+      next_stage(n, cy, tl);
+      load_probs(n, cy, tl, pn);  // in flight while this cell row is scattered
+      uint8_t* col = sPt + pb * kPtBytes + (t >> 3) * 128 + (t & 7) * 2;
+      if (t < kKc) {
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          const int e = pb ? prev1[k] : prev0[k];
+          if (e >= 0) *reinterpret_cast<uint16_t*>(col + (e >> 3) * kPtSbo + (e & 7) * 16) = 0;
+        }
+        int nk[K];
+#pragma unroll
+        for (int k = 0; k < K; ++k) nk[k] = -1;
+        const int ox = 2 * (ctl.vx0 - kPn) + px;
+        if (ox >= 0 && ox < 2 * p.W) {
+          const int cx = ox >> 1;
+          bool border = false;
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+            const int yy = ccy + p.dy[k], xx = cx + p.dx[k];
+            border |= yy < 0 || yy >= p.H || xx < 0 || xx >= p.W;
+            const int ny = min(max(yy, 0), p.H - 1) - ctl.vy0, nx = min(max(xx, 0), p.W - 1) - ctl.vx0;
+            nk[k] = (ny >= 0 && ny < kTy && nx >= 0 && nx < kTx) ? ny * kTx + nx : -1;
+          }
+          if (border) {  // offsets that clamp onto the same value pixel are summed in fp32
+#pragma unroll
+            for (int k = 1; k < K; ++k) {
+#pragma unroll
+              for (int j = 0; j < k; ++j) {
+                if (nk[k] >= 0 && nk[j] == nk[k]) {
+                  pk[j] += pk[k];
+                  nk[k] = -1;
                 }
               }
             }
-            uint8_t* col = buf + (t >> 3) * 128 + (t & 7) * 2;
-#pragma unroll
-            for (int k = 0; k < K; ++k)
-              if (nk[k] >= 0)
-                *reinterpret_cast<uint16_t*>(col + (nk[k] >> 3) * kPtSbo + (nk[k] & 7) * 16) = S::bits(pk[k]);
           }
+#pragma unroll
+          for (int k = 0; k < K; ++k)
+            if (nk[k] >= 0)
+              *reinterpret_cast<uint16_t*>(col + (nk[k] >> 3) * kPtSbo + (nk[k] & 7) * 16) = S::bits(pk[k]);
         }
-        fence_proxy_async();  // Pt is read by the tensor core (async proxy)
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&pt_full[pb]);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          if (pb) prev1[k] = (int8_t)nk[k];
+          else prev0[k] = (int8_t)nk[k];
+        }
       }
+      fence_proxy_async();  // Pt is read by the tensor core (async proxy)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pt_full[pb]);
+      ++gc;
     }
   } else {
     // ------------------------------------------------------------ epilogue
