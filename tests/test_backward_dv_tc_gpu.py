@@ -4,7 +4,9 @@ rows that reach the tile, Pt (the softmax weights, rounded to the storage
 type) built in shared memory.  It is the transpose of the forward's pooling
 (uplift/uplift.py:835-837), so it is checked against fp64 autograd through
 the oracle (every K, ragged tiles, 1-6 channel chunks, permuted offset
-tables, hardmax, fp16), and against the CUDA-core dV kernel it replaces
+tables, hardmax, fp16; border tiles through the scatter fill of Pt,
+interior tiles through the gather fill), and against the CUDA-core dV
+kernel it replaces
 (ULA_BWD_DV_TC=0, read once per process, so that run is a child process)."""
 import os
 import subprocess
@@ -58,9 +60,11 @@ def _kernel_dv(case, offsets, pn, hardmax):
 @pytest.mark.parametrize("K", [5, 9, 13, 17, 25])
 def test_tc_dv_vs_fp64_autograd(K, cuda_lib):
     offsets, pn = neighbourhood(K)
-    # (B, C, H, W): ragged tiles (H % 8, W % 16), tiny maps, 1-6 chunks
+    # (B, C, H, W): ragged tiles (H % 8, W % 16), tiny maps, 1-6 chunks;
+    # the last three have interior tiles (no value pixel on the map border:
+    # the gather fill of Pt), the smallest such maps among them
     for i, (B, C, H, W) in enumerate([(2, 64, 5, 7), (1, 384, 9, 17), (2, 128, 8, 16), (1, 192, 1, 1),
-                                      (1, 320, 12, 40)]):
+                                      (1, 320, 12, 40), (2, 64, 17, 33), (1, 128, 24, 50), (1, 384, 33, 70)]):
         case = _case(K, B, C, H, W, seed=K * 7 + i, dt=torch.bfloat16)
         err = normwise_err(_kernel_dv(case, offsets, pn, False), _oracle_dv(case, offsets, pn, False))
         assert err <= TOL16[torch.bfloat16], (K, B, C, H, W, err)
@@ -70,10 +74,11 @@ def test_tc_dv_permuted_offsets_hardmax_fp16(cuda_lib):
     offsets, pn = neighbourhood(17)
     perm = offsets[9:] + offsets[:9]
     for dt in (torch.bfloat16, torch.float16):
-        case = _case(17, 2, 128, 10, 19, seed=3, dt=dt, wscale=0.05)
-        for offs, hard in ((perm, False), (offsets, True), (perm, True)):
-            err = normwise_err(_kernel_dv(case, offs, pn, hard), _oracle_dv(case, offs, pn, hard))
-            assert err <= TOL16[dt], (dt, hard, err)
+        for shape in ((2, 128, 10, 19), (1, 128, 26, 49)):  # border tiles only; interior tiles too
+            case = _case(17, *shape, seed=3, dt=dt, wscale=0.05)
+            for offs, hard in ((perm, False), (offsets, True), (perm, True)):
+                err = normwise_err(_kernel_dv(case, offs, pn, hard), _oracle_dv(case, offs, pn, hard))
+                assert err <= TOL16[dt], (dt, shape, hard, err)
 
 
 SCRIPT = r"""

@@ -23,9 +23,9 @@
 //
 // Roles (320 threads, one CTA per SM, persistent over tiles): warp 0 TMA
 // producer of the dout ring; warp 1 TMEM owner + MMA issuer; warps 2-5 build
-// Pt (double-buffered; each thread owns a column, clears its own earlier
-// entries instead of a zero pass, and loads the next cell row's weights
-// while scattering the current one); warps 6-9 epilogue (TMEM -> storage type -> swizzled
+// Pt (double-buffered; interior tiles by a gather, a thread per Pt row with
+// the next cell row's weights loaded ahead, border tiles by a scatter with
+// clamped duplicates summed); warps 6-9 epilogue (TMEM -> storage type -> swizzled
 // staging -> TMA store of the warp's 2 value rows).  Every mbarrier wait is
 // bounded; on expiry the CTA records the role in this kernel's status word
 // (and the registered host word), drains and exits.
@@ -84,6 +84,8 @@ struct Params {
   const float* probs; // [B][2H][2W][K] fp32
   int8_t dy[UPLIFT_LA_MAX_K];
   int8_t dx[UPLIFT_LA_MAX_K];
+  int8_t ktab[(2 * kPn + 1) * (2 * kPn + 1)];  // offset (dy, dx) -> k, or -1
+  int gather;                                  // 1: the offsets are distinct (the gather fill applies)
   int B, C, H, W, K, nchunks, tiles_x, tiles_y, num_tiles;
   uint64_t timeout_ns;
   unsigned int* host_status;
@@ -244,17 +246,49 @@ __global__ void __launch_bounds__(kThreads, 1) la_dv_tc_kernel(const __grid_cons
     }
   } else if (warp < 6) {
     // ------------------------------------------------------------ Pt builders
-    // thread t < 80 owns output pixel t of the cell row (2 rows x 40
-    // columns), i.e. column t of Pt: it scatters that pixel's softmax
-    // weights into its column, and before that clears the entries it set
-    // in the same buffer two cell rows earlier (both buffers are zeroed
-    // once at the start), so no thread waits for another.  The weights of
-    // the next cell row are loaded while the current one is scattered.
+    // Two ways to fill a cell row's Pt buffer; all four warps take the same
+    // one for a tile.
+    //  * gather (tiles with no value pixel on the map border, distinct
+    //    offsets): thread t owns row t of Pt, value pixel (vy, vx) =
+    //    (vy0 + t / 16, vx0 + t % 16).  Cell row cy reaches it only through
+    //    the offset row dy = vy - cy, from the 5 cells cx = vx - dx, each with
+    //    its 2 x 2 output pixels; no clamping can send anything else there.
+    //    The thread writes its whole row (zeros, then the 10 packed pairs), so
+    //    nothing is left from earlier cell rows, and the 20 weights of the
+    //    next cell row are loaded while this one is written.
+    //  * scatter (border tiles, where clamping sends several offsets of one
+    //    output pixel to one value pixel): the buffer is zeroed, then thread
+    //    t < 80 scatters output pixel t's weights into column t of Pt,
+    //    summing the clamped duplicates in fp32.
+    // One thread waits on the buffer's barrier and shares the outcome (in
+    // a per-buffer word, so a slow reader never sees the next cell row's),
+    // so all take the same path.
     const int t = tid - 64;
-    const int py = t / (2 * kRegX), px = t - py * (2 * kRegX);
-    for (int i = t; i < 2 * kPtBytes / 16; i += 128) reinterpret_cast<uint4*>(sPt)[i] = make_uint4(0, 0, 0, 0);
-    named_bar(1, 128);
-    // the stage after (n, cy): next cell row of the tile, else the next tile's first
+    const int rny = t >> 4, rnx = t & 15;
+    auto interior = [&](const Tile& tl) {
+      return p.gather != 0 && tl.vy0 >= 1 && tl.vy0 + kTy <= p.H - 1 && tl.vx0 >= 1 && tl.vx0 + kTx <= p.W - 1;
+    };
+    // the 20 weights of row t for cell row cy: [cell j][output row][output column]
+    auto gather_load = [&](int cy, const Tile& tl, float* g) {
+#pragma unroll
+      for (int i = 0; i < 20; ++i) g[i] = 0.f;
+      const int dyv = tl.vy0 + rny - cy;
+      if (dyv < -kPn || dyv > kPn) return;
+#pragma unroll
+      for (int j = 0; j < 2 * kPn + 1; ++j) {  // cell column vx - dx with dx = kPn - j
+        const int k = p.ktab[(dyv + kPn) * (2 * kPn + 1) + (2 * kPn - j)];
+        const int cx = tl.vx0 - kPn + rnx + j;
+        if (k >= 0 && cx < p.W) {
+          const float* pr = p.probs + (((int64_t)tl.b * 2 * p.H + 2 * cy) * (2 * p.W) + 2 * cx) * K + k;
+          const int64_t rs = (int64_t)2 * p.W * K;
+          g[4 * j + 0] = __ldg(pr);
+          g[4 * j + 1] = __ldg(pr + K);
+          g[4 * j + 2] = __ldg(pr + rs);
+          g[4 * j + 3] = __ldg(pr + rs + K);
+        }
+      }
+    };
+    // next stage after (n, cy): the next cell row of the tile, else the next tile's first
     auto next_stage = [&](int& n, int& cy, Tile& tl) {
       if (++cy >= tl.r1) {
         if (++n < local_tiles) {
@@ -263,81 +297,85 @@ __global__ void __launch_bounds__(kThreads, 1) la_dv_tc_kernel(const __grid_cons
         }
       }
     };
-    auto load_probs = [&](int n, int cy, const Tile& tl, float* dst) {
-      const int oy = 2 * cy + py, ox = 2 * (tl.vx0 - kPn) + px;
-      if (n < local_tiles && t < kKc && ox >= 0 && ox < 2 * p.W) {
-        const float* pr = p.probs + (((int64_t)tl.b * 2 * p.H + oy) * (2 * p.W) + ox) * K;
-#pragma unroll
-        for (int k = 0; k < K; ++k) dst[k] = __ldg(pr + k);
-      }
-    };
-    int8_t prev0[K], prev1[K];  // the entries this thread set in buffer 0 / 1
-#pragma unroll
-    for (int k = 0; k < K; ++k) prev0[k] = prev1[k] = -1;
-    float pk[K], pn[K];
-#pragma unroll
-    for (int k = 0; k < K; ++k) pk[k] = pn[k] = 0.f;
+    float gcur[20], gnext[20];
     int n = 0, cy = 0;
     Tile tl{};
+    bool g_next = false;
     if (local_tiles > 0) {
       tl = tile_of(p, blockIdx.x);
       cy = tl.r0;
-      load_probs(n, cy, tl, pn);
+      g_next = interior(tl);
+      if (g_next) gather_load(cy, tl, gnext);
     }
     uint32_t gc = 0;
     while (n < local_tiles) {
       const int pb = gc & 1;
-      int ok = 0;
-      if (lane == 0) ok = mbar_wait(&pt_empty[pb], ((gc >> 1) & 1) ^ 1, abort_flag, 3, tmo) ? 1 : 0;
-      if (__shfl_sync(0xffffffffu, ok, 0) == 0) break;
-#pragma unroll
-      for (int k = 0; k < K; ++k) pk[k] = pn[k];
+      if (t == 0) go[pb] = mbar_wait(&pt_empty[pb], ((gc >> 1) & 1) ^ 1, abort_flag, 3, tmo) ? 1 : 0;
+      named_bar(1, 128);
+      if (go[pb] == 0) break;
       const int ccy = cy;
       const Tile ctl = tl;
+      const bool gather = g_next;
+      if (gather) {
+#pragma unroll
+        for (int i = 0; i < 20; ++i) gcur[i] = gnext[i];
+      }
       next_stage(n, cy, tl);
-      load_probs(n, cy, tl, pn);  // in flight while this cell row is scattered
-      uint8_t* col = sPt + pb * kPtBytes + (t >> 3) * 128 + (t & 7) * 2;
-      if (t < kKc) {
+      g_next = n < local_tiles && interior(tl);
+      if (g_next) gather_load(cy, tl, gnext);  // in flight while this cell row is written
+      uint8_t* buf = sPt + pb * kPtBytes;
+      if (gather) {
+        // row t: 10 groups of 8 K-elements, 128 bytes apart
+        uint8_t* row = buf + (t >> 3) * kPtSbo + (t & 7) * 16;
 #pragma unroll
-        for (int k = 0; k < K; ++k) {
-          const int e = pb ? prev1[k] : prev0[k];
-          if (e >= 0) *reinterpret_cast<uint16_t*>(col + (e >> 3) * kPtSbo + (e & 7) * 16) = 0;
-        }
-        int nk[K];
+        for (int q = 0; q < kKc / 8; ++q) *reinterpret_cast<uint4*>(row + q * 128) = make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int k = 0; k < K; ++k) nk[k] = -1;
-        const int ox = 2 * (ctl.vx0 - kPn) + px;
-        if (ox >= 0 && ox < 2 * p.W) {
-          const int cx = ox >> 1;
-          bool border = false;
+        for (int j = 0; j < 2 * kPn + 1; ++j) {
 #pragma unroll
-          for (int k = 0; k < K; ++k) {
-            const int yy = ccy + p.dy[k], xx = cx + p.dx[k];
-            border |= yy < 0 || yy >= p.H || xx < 0 || xx >= p.W;
-            const int ny = min(max(yy, 0), p.H - 1) - ctl.vy0, nx = min(max(xx, 0), p.W - 1) - ctl.vx0;
-            nk[k] = (ny >= 0 && ny < kTy && nx >= 0 && nx < kTx) ? ny * kTx + nx : -1;
+          for (int py = 0; py < 2; ++py) {
+            const int pc = py * (2 * kRegX) + 2 * (rnx + j);  // K index (output pixel) of the pair, even
+            *reinterpret_cast<uint32_t*>(row + (pc >> 3) * 128 + (pc & 7) * 2) =
+                S::pack(gcur[4 * j + 2 * py], gcur[4 * j + 2 * py + 1]);
           }
-          if (border) {  // offsets that clamp onto the same value pixel are summed in fp32
+        }
+      } else {
+        for (int i = t; i < kPtBytes / 16; i += 128) reinterpret_cast<uint4*>(buf)[i] = make_uint4(0, 0, 0, 0);
+        named_bar(1, 128);
+        if (t < kKc) {
+          const int py = t / (2 * kRegX), px = t - py * (2 * kRegX);
+          const int oy = 2 * ccy + py, ox = 2 * (ctl.vx0 - kPn) + px;
+          if (ox >= 0 && ox < 2 * p.W) {
+            const int cx = ox >> 1;
+            const float* pr = p.probs + (((int64_t)ctl.b * 2 * p.H + oy) * (2 * p.W) + ox) * K;
+            float pk[K];
+            int nk[K];
+            bool border = false;
 #pragma unroll
-            for (int k = 1; k < K; ++k) {
+            for (int k = 0; k < K; ++k) {
+              pk[k] = __ldg(pr + k);
+              const int yy = ccy + p.dy[k], xx = cx + p.dx[k];
+              border |= yy < 0 || yy >= p.H || xx < 0 || xx >= p.W;
+              const int ny = min(max(yy, 0), p.H - 1) - ctl.vy0, nx = min(max(xx, 0), p.W - 1) - ctl.vx0;
+              nk[k] = (ny >= 0 && ny < kTy && nx >= 0 && nx < kTx) ? ny * kTx + nx : -1;
+            }
+            if (border) {  // offsets that clamp onto the same value pixel are summed in fp32
 #pragma unroll
-              for (int j = 0; j < k; ++j) {
-                if (nk[k] >= 0 && nk[j] == nk[k]) {
-                  pk[j] += pk[k];
-                  nk[k] = -1;
+              for (int k = 1; k < K; ++k) {
+#pragma unroll
+                for (int j = 0; j < k; ++j) {
+                  if (nk[k] >= 0 && nk[j] == nk[k]) {
+                    pk[j] += pk[k];
+                    nk[k] = -1;
+                  }
                 }
               }
             }
+            uint8_t* col = buf + (t >> 3) * 128 + (t & 7) * 2;
+#pragma unroll
+            for (int k = 0; k < K; ++k)
+              if (nk[k] >= 0)
+                *reinterpret_cast<uint16_t*>(col + (nk[k] >> 3) * kPtSbo + (nk[k] & 7) * 16) = S::bits(pk[k]);
           }
-#pragma unroll
-          for (int k = 0; k < K; ++k)
-            if (nk[k] >= 0)
-              *reinterpret_cast<uint16_t*>(col + (nk[k] >> 3) * kPtSbo + (nk[k] & 7) * 16) = S::bits(pk[k]);
-        }
-#pragma unroll
-        for (int k = 0; k < K; ++k) {
-          if (pb) prev1[k] = (int8_t)nk[k];
-          else prev0[k] = (int8_t)nk[k];
         }
       }
       fence_proxy_async();  // Pt is read by the tensor core (async proxy)
@@ -463,6 +501,13 @@ int dv_tc_launch(const DvArgs& a, cudaStream_t stream) {
   for (int k = 0; k < a.K; ++k) {
     p.dy[k] = a.dy[k];
     p.dx[k] = a.dx[k];
+  }
+  memset(p.ktab, 0xff, sizeof(p.ktab));
+  p.gather = 1;
+  for (int k = 0; k < a.K; ++k) {
+    int8_t& e = p.ktab[(a.dy[k] + kPn) * (2 * kPn + 1) + (a.dx[k] + kPn)];
+    if (e >= 0) p.gather = 0;  // a repeated offset: its weights would have to be summed
+    e = (int8_t)k;
   }
   p.B = a.B; p.C = a.C; p.H = a.H; p.W = a.W; p.K = a.K;
   p.nchunks = a.C / kChunk;
