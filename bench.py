@@ -606,8 +606,9 @@ def run_backward(dev, stream, peak, images, reps=5):
     `ms_eager` is one eager call from the host, median of `reps` (it adds
     the Python wrapper's launch latency).  Algorithmic bytes per output
     pixel: dout + guide read, dguide written ((C + 2 Cg) * 2), the fp32
-    softmax workspace written once and read twice (12 K), value read and
-    dvalue written once per value pixel (2 C * 2 / 4)."""
+    softmax workspace written by the dlogit kernel and read once by the dV
+    kernel (8 K), value read and dvalue written once per value pixel
+    (2 C * 2 / 4); dout's second read (by the dV kernel) is not counted."""
     from uplift_b200 import ops
     from uplift_b200.attender import LocalAttender, neighbourhood
 
@@ -618,7 +619,7 @@ def run_backward(dev, stream, peak, images, reps=5):
     b = la.conv1.bias.detach().float()
     g = torch.Generator().manual_seed(0)
     cl = torch.channels_last
-    bpp = (C + 2 * CG) * ELEM + 12 * K_NBR + 2 * C * ELEM / 4
+    bpp = (C + 2 * CG) * ELEM + 8 * K_NBR + 2 * C * ELEM / 4
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     cap = torch.cuda.Stream(dev)  # graphs are captured off the default stream
     levels, tot_ms, tot_px, tot_eager = [], 0.0, 0, 0.0
