@@ -320,6 +320,13 @@ def run_ours(args, world, rank, local):
     # ---- attender backward (training) on the same four levels
     bwd = None if args.no_backward else run_backward(dev, stream, peak, B_PER_GPU)
 
+    # ---- the reference's own upsampler (make_fast + torch.compile), N=1 only,
+    # after every timing of this repository's kernels (its compile sets global
+    # TF32 switches; they are restored)
+    ref_ups = None
+    if world == 1 and not args.no_upsampler and not args.no_ref_upsampler:
+        ref_ups = run_reference_upsampler(dev, stream, True)
+
     # ---- CPU baseline (rank 0, N=1 only): reference algorithm on host cores
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -361,6 +368,8 @@ def run_ours(args, world, rank, local):
         result["fused_resize"] = fused_rs
     if bwd is not None:
         result["backward"] = bwd
+    if ref_ups is not None:
+        result["reference_upsampler"] = ref_ups
     if cpu is not None:
         result["cpu_baseline"] = cpu
     result["summary"] = summary(result)
@@ -381,6 +390,7 @@ def summary(r):
             "e2e_Mpix_s": get("e2e", "value"), "e2e_copy_frac": get("e2e", "copy_roofline", "e2e_frac"),
             "triton_ref_Mpix_s": get("triton_reference", "Mpix_s"),
             "cfg5_img_s": get("upsampler", "img_per_s"),
+            "cfg5_ref_compiled_img_s": get("reference_upsampler", "img_per_s"),
             "fused_resize_speedup": get("fused_resize", "speedup"),
             "cfg5_img_s_gather": get("upsampler", "gather", "img_per_s"),
             "cfg3_img_s": get("upsampler_other_configs", "dinov3_splus16_512_b32_bf16", "img_per_s"),
@@ -1010,6 +1020,84 @@ def run_gather(fast, dev, stream, world, rank, global_images, mine, lo, img, fea
                    "micro-batch's forward (2 CUDA-graph slots); only rank 0 holds the full batch"}
 
 
+def run_reference_upsampler(dev, stream, compile_model, images=16, micro_batch=8, min_ms=400.0):
+    """The reference's own upsampler on the 1022 px DINOv2 configuration
+    (config 5: image 1022^2, features 384 x 73^2, iters=4, output 1022^2,
+    bf16): its UPLiFT (uplift/uplift.py:538-) built from its shipped
+    uplift_dinov2-s14.yaml with random init, wrapped by its make_fast
+    (uplift/fast.py:71-133: BatchNorm folding, channels_last, the Triton
+    attender, and with `compile_model` torch.compile in its default
+    max-autotune mode), unmodified from the baseline/_ref install.  One GPU,
+    micro-batches of `micro_batch` images resident on the device; the first
+    call (compilation and autotuning) is timed on its own, then passes of
+    `images` images are timed with CUDA events for ~`min_ms`.  make_fast
+    turns TF32 on globally when it compiles (uplift/fast.py:122-124); the
+    previous settings are restored after."""
+    import time
+    from types import SimpleNamespace
+    import yaml
+    mods, why = reference_modules("uplift", "fast")
+    if not mods:
+        return {"unavailable": why}
+    up, fastmod = mods
+
+    def ns(d):
+        if isinstance(d, dict):
+            return SimpleNamespace(**{k: ns(v) for k, v in d.items()})
+        if isinstance(d, list):
+            return [ns(v) for v in d]
+        return d
+
+    cfg = ns(yaml.safe_load(open(REF_ROOT / "uplift" / "configs" / "uplift_dinov2-s14.yaml")))
+    tf32 = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+    try:
+        torch.manual_seed(0)
+        model = up.UPLiFT(cfg.backbone.channel, cfg.backbone.patch, cfg.uplift, dtype=torch.bfloat16).eval()
+        model.enable_iterative(4)
+        fast = fastmod.make_fast(model, compile=compile_model, warmup=False, device=dev)
+        g = torch.Generator().manual_seed(1000)
+        img = torch.rand(micro_batch, 3, 1022, 1022, generator=g).to(torch.bfloat16).to(dev)
+        feats = torch.randn(micro_batch, cfg.backbone.channel, 73, 73, generator=g).to(torch.bfloat16).to(dev)
+        img = img.contiguous(memory_format=torch.channels_last)
+        feats = feats.contiguous(memory_format=torch.channels_last)
+        n_mb = -(-images // micro_batch)
+        with torch.cuda.stream(stream):
+            t0 = time.time()
+            fast(img, feats, [1022, 1022])
+            torch.cuda.synchronize(dev)
+            first_s = time.time() - t0
+            for _ in range(2):
+                fast(img, feats, [1022, 1022])
+
+            def one_pass():
+                for _ in range(n_mb):
+                    fast(img, feats, [1022, 1022])
+
+            def timed(passes):
+                torch.cuda.synchronize(dev)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(passes):
+                    one_pass()
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+                return e0.elapsed_time(e1) / passes
+
+            ms = timed(1)
+            passes = int(max(2, min(20, -(-min_ms // max(ms, 1e-3)))))
+            ms = timed(passes)
+    except Exception as e:  # noqa: BLE001 -- reported, not raised: the bench line still prints
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = tf32
+    return {"img_per_s": round(n_mb * micro_batch / (ms / 1e3), 2), "ms_per_pass": round(ms, 2),
+            "images_per_pass": n_mb * micro_batch, "micro_batch": micro_batch, "passes": passes,
+            "first_call_s": round(first_s, 1),
+            "path": "reference UPLiFT + make_fast(compile=%s%s) from baseline/_ref, unmodified, bf16, "
+                    "random init, eager CUDA-event timing of passes" % (compile_model,
+                                                                        ", mode max-autotune" if compile_model else "")}
+
+
 def run_model_configs(dev, stream, world, rank, args):
     """The other two model configurations, whole upsampler, batch-sharded:
     DINOv3-S+/16 at 512 px (features 384 x 32^2, iters=4, outsize 512,
@@ -1161,6 +1249,10 @@ def main():
                     help="run only the whole-upsampler pass (profiling captures)")
     ap.add_argument("--only-fused-resize", action="store_true",
                     help="run only the fused attender + final resize timing (profiling captures; --images)")
+    ap.add_argument("--no-ref-upsampler", action="store_true",
+                    help="skip timing the reference's own compiled upsampler (N=1)")
+    ap.add_argument("--only-reference-upsampler", action="store_true",
+                    help="run only the reference's own make_fast upsampler at 1022 px, eager and compiled")
     ap.add_argument("--images", type=int, default=8,
                     help="images per GPU (default 8; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -1186,6 +1278,11 @@ def main():
             dev = torch.device("cuda", local)
             res = {"fused_resize": run_fused_resize(dev, torch.cuda.current_stream(dev), load_peaks()[0],
                                                     images=B_PER_GPU)}
+        elif args.only_reference_upsampler:
+            dev = torch.device("cuda", local)
+            st = torch.cuda.current_stream(dev)
+            res = {"reference_upsampler": {"eager": run_reference_upsampler(dev, st, False),
+                                           "compiled": run_reference_upsampler(dev, st, True)}}
         elif args.only_upsampler:
             dev = torch.device("cuda", local)
             res = {"upsampler": run_upsampler(dev, torch.cuda.current_stream(dev), world, rank, args, outsize=1022,
