@@ -943,7 +943,8 @@ def run_upsampler(dev, stream, world, rank, args, variant="dinov2-s14", img_px=1
         gat = None
         if gather and world > 1:
             gat = run_gather(fast, dev, stream, world, rank, global_images, mine, lo, img, feats, size,
-                             dtype, out_shape, min(gather_micro_batch, mb), timed, passes_for)
+                             dtype, out_shape, min(max(gather_micro_batch, getattr(args, "gather_groups", 1)), mb),
+                             timed, passes_for, getattr(args, "gather_ctas", 0), getattr(args, "gather_groups", 1))
     del fast, model, img, feats
     torch.cuda.empty_cache()
     dt = {torch.bfloat16: "bf16", torch.float32: "fp32"}[dtype]
@@ -960,60 +961,90 @@ def run_upsampler(dev, stream, world, rank, args, variant="dinov2-s14", img_px=1
 
 
 def run_gather(fast, dev, stream, world, rank, global_images, mine, lo, img, feats, size, dtype, out_shape,
-               gmb, timed, passes_for):
+               gmb, timed, passes_for, gather_ctas=0, gather_groups=1):
     """Upsampler timing with the final gather of every output to rank 0 (see
     run_upsampler).  Shards are equal (global batch divisible by the world
-    size), so every rank issues the same gathers in the same order."""
+    size), so every rank issues the same gathers in the same order.
+
+    gather_ctas > 0: the gathers run on their own NCCL communicator capped at
+    that many CTAs, and this package's persistent kernels leave as many SMs
+    to them (uplift_la_set_max_ctas, set before the graphs are captured: the
+    grid is part of them), so that the transfer and the forward share the
+    GPU instead of queueing for SMs."""
     import torch.distributed as dist
+    from uplift_b200 import _native
     from uplift_b200.sharding import shard_bounds
     C, H, W = out_shape
     bounds = [shard_bounds(global_images, r, world) for r in range(world)]
     if len({hi - lo_ for lo_, hi in bounds}) != 1 or mine % gmb != 0:
         return {"skipped": "unequal shards"}
-    full = None
-    if rank == 0:
-        full = torch.empty((global_images, C, H, W), dtype=dtype, device=dev, memory_format=torch.channels_last)
-    n_mb = mine // gmb
-    x_img, x_feats = img[:gmb], feats[:gmb]
-    pool = torch.cuda.graph_pool_handle()
-    graphs, outs = [], []
-    for _ in range(2):  # two slots: one is gathered while the other is computed
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            fast(x_img, x_feats, size)
-        stream.wait_stream(side)
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, pool=pool):
-            outs.append(fast(x_img, x_feats, size))
-        graphs.append(gr)
-    torch.cuda.synchronize(dev)
+    # one communicator per concurrent gather: each image of a micro-batch is
+    # gathered on its own (round-robin over the groups), so up to
+    # gather_groups transfers run at once on separate NCCL streams
+    groups = [None]
+    if gather_ctas > 0 or gather_groups > 1:
+        groups = []
+        for _ in range(max(1, gather_groups)):
+            opts = dist.ProcessGroupNCCL.Options()
+            if gather_ctas > 0:
+                opts.config.max_ctas = gather_ctas
+            groups.append(dist.new_group(backend="nccl", pg_options=opts))
+    if gather_ctas > 0:
+        _native.set_max_ctas(max(1, torch.cuda.get_device_properties(dev).multi_processor_count - gather_ctas))
+    try:
+        full = None
+        if rank == 0:
+            full = torch.empty((global_images, C, H, W), dtype=dtype, device=dev, memory_format=torch.channels_last)
+        n_mb = mine // gmb
+        x_img, x_feats = img[:gmb], feats[:gmb]
+        pool = torch.cuda.graph_pool_handle()
+        graphs, outs = [], []
+        for _ in range(2):  # two slots: one is gathered while the other is computed
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                fast(x_img, x_feats, size)
+            stream.wait_stream(side)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, pool=pool):
+                outs.append(fast(x_img, x_feats, size))
+            graphs.append(gr)
+        torch.cuda.synchronize(dev)
 
-    def nhwc(t):  # a contiguous view of a channels_last tensor, as NCCL wants it
-        return t.permute(0, 2, 3, 1)
+        def nhwc(t):  # a contiguous view of a channels_last tensor, as NCCL wants it
+            return t.permute(0, 2, 3, 1)
 
-    def gather_pass():
-        pending = [None, None]
-        for j in range(n_mb):
-            sl = j & 1
-            if pending[sl] is not None:
-                pending[sl].wait()  # the stream waits until that gather has read the slot
-            graphs[sl].replay()
-            parts = None
-            if rank == 0:
-                parts = [nhwc(full[lo_ + j * gmb: lo_ + (j + 1) * gmb]) for lo_, _ in bounds]
-            pending[sl] = dist.gather(nhwc(outs[sl]), gather_list=parts, dst=0, async_op=True)
-        for w in pending:
-            if w is not None:
-                w.wait()
-    ms = timed(gather_pass, 1)
-    passes = passes_for(ms)
-    ms = timed(gather_pass, passes)
-    del graphs, outs, full
+        def gather_pass():
+            pending = [[], []]
+            for j in range(n_mb):
+                sl = j & 1
+                for w in pending[sl]:
+                    w.wait()  # the stream waits until that gather has read the slot
+                pending[sl] = []
+                graphs[sl].replay()
+                per = gmb if len(groups) == 1 else 1
+                for i0 in range(0, gmb, per):
+                    parts = None
+                    if rank == 0:
+                        parts = [nhwc(full[lo_ + j * gmb + i0: lo_ + j * gmb + i0 + per]) for lo_, _ in bounds]
+                    pending[sl].append(dist.gather(nhwc(outs[sl][i0:i0 + per]), gather_list=parts, dst=0,
+                                                   group=groups[(i0 // per) % len(groups)], async_op=True))
+            for ws in pending:
+                for w in ws:
+                    w.wait()
+        ms = timed(gather_pass, 1)
+        passes = passes_for(ms)
+        ms = timed(gather_pass, passes)
+        del graphs, outs, full
+    finally:
+        if gather_ctas > 0:
+            _native.set_max_ctas(0)
     elem = 2 if dtype != torch.float32 else 4
     into_root = (world - 1) * mine * C * H * W * elem
     return {"img_per_s": round(global_images / (ms / 1e3), 2), "ms_per_global_batch": round(ms, 2),
             "passes": passes, "gather_micro_batch": gmb,
+            "gather_ctas": gather_ctas or "NCCL default (attender on every SM)",
+            "gather_groups": len(groups),
             "bytes_into_rank0_per_batch": into_root,
             "rank0_ingress_GB_s": round(into_root / (ms / 1e3) / 1e9, 1),
             "how": "NCCL gather per micro-batch into rank 0's [global, C, H, W] tensor, overlapping the next "
@@ -1249,6 +1280,10 @@ def main():
                     help="run only the whole-upsampler pass (profiling captures)")
     ap.add_argument("--only-fused-resize", action="store_true",
                     help="run only the fused attender + final resize timing (profiling captures; --images)")
+    ap.add_argument("--gather-ctas", type=int, default=0,
+                    help="N>1: CTAs for the gather's own NCCL communicator, left free by the attender (0: none)")
+    ap.add_argument("--gather-groups", type=int, default=1,
+                    help="N>1: concurrent NCCL communicators for the gather (one image per transfer)")
     ap.add_argument("--no-ref-upsampler", action="store_true",
                     help="skip timing the reference's own compiled upsampler (N=1)")
     ap.add_argument("--only-reference-upsampler", action="store_true",

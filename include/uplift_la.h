@@ -273,6 +273,14 @@ int uplift_la_set_host_status_word(unsigned int* word);
  * counterpart. */
 int uplift_la_test_hook(int fault, unsigned long long wait_limit_ns);
 
+/* At most n CTAs (0: one per SM, the default) for the persistent
+ * tensor-core kernels (forward and backward; each holds a whole SM).  For a
+ * caller that runs communication kernels beside them -- an NCCL gather of
+ * the previous batch's output, say -- so that those get SMs without
+ * delaying the attender's CTAs.  Process-wide, takes effect at the next
+ * launch; n < 0 is UPLIFT_LA_ERR_ARG.  No reference counterpart. */
+int uplift_la_set_max_ctas(int n);
+
 /* Message for the last non-OK status returned on the calling thread. */
 const char* uplift_la_last_error(void);
 

@@ -73,6 +73,14 @@ def test_validation_errors_without_launch(lib):
     assert _call_forward(lib, vs=s, os=s, gs=s) == _native.ERR_ARG
 
 
+def test_cta_limit_is_validated(lib):
+    """uplift_la_set_max_ctas: n < 0 is an argument error; 0 restores one CTA
+    per SM (host-side state only, no device touched)."""
+    assert lib.uplift_la_set_max_ctas(-1) == _native.ERR_ARG
+    assert lib.uplift_la_set_max_ctas(37) == _native.OK
+    assert lib.uplift_la_set_max_ctas(0) == _native.OK
+
+
 def test_empty_problem_is_a_noop(lib):
     """B = 0: validated and returns OK without touching a device."""
     s = (ctypes.c_int64 * 4)(32, 1, 16, 8)

@@ -120,6 +120,33 @@ def test_policy_errors(cuda_lib):
     assert kernel in _native.KERNELS_CUDA_CORE
 
 
+def test_cta_limit_leaves_results_unchanged(cuda_lib):
+    """uplift_la_set_max_ctas caps the persistent kernels' grid (for running
+    communication kernels beside them): every tile is computed the same way
+    by whichever CTA takes it, so the forward and the backward are bitwise
+    identical under a cap of 37 CTAs."""
+    guide, value, weight, bias = _inputs(2, 20, 36, 384, 17, torch.bfloat16, seed=31)
+    offsets, pn = neighbourhood(17)
+    cl = torch.channels_last
+    g, v = guide.to(DEV).contiguous(memory_format=cl), value.to(DEV).contiguous(memory_format=cl)
+    dout = torch.randn(2, 384, 40, 72, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
+    dout = dout.to(DEV).contiguous(memory_format=cl)
+
+    def run():
+        out = ops.local_attender_raw(g, v, weight.to(DEV), bias.to(DEV), offsets, pn)
+        dg, dv, dw, db = ops.local_attender_backward_raw(dout, g, v, weight.to(DEV), bias.to(DEV), offsets, pn)
+        torch.cuda.synchronize()
+        return out, dg, dv
+    full = run()
+    try:
+        _native.set_max_ctas(37)
+        capped = run()
+    finally:
+        _native.set_max_ctas(0)
+    for a, b in zip(full, capped):
+        assert torch.equal(a, b)
+
+
 def test_expired_wait_is_reported_and_context_survives(cuda_lib):
     """Failure detection without a GPU fault: the test hook makes the guide
     producer issue no loads, so the consumers' bounded waits (limited to

@@ -33,6 +33,7 @@ EXPORTED = (
     "uplift_la_device_status",
     "uplift_la_test_hook",
     "uplift_la_set_host_status_word",
+    "uplift_la_set_max_ctas",
     "uplift_la_backward",
     "uplift_la_backward_noalloc",
     # include/uplift_glue.h
@@ -107,6 +108,8 @@ def load(build_if_missing: bool = False):
         lib.uplift_la_test_hook.argtypes = [i, ctypes.c_ulonglong]
         lib.uplift_la_set_host_status_word.restype = i
         lib.uplift_la_set_host_status_word.argtypes = [vp]
+        lib.uplift_la_set_max_ctas.restype = i
+        lib.uplift_la_set_max_ctas.argtypes = [i]
         lib.uplift_la_backward.restype = i
         lib.uplift_la_backward.argtypes = [vp, i64p, vp, i64p, vp, i64p, fp, fp, fp, vp, i64p, vp, i64p,
                                            fp, fp, i, i, i, i, i, i, i, i8p, i, i, i, i, vp]
@@ -166,6 +169,13 @@ class kernel_policy:
 
 def last_kernel() -> int:
     return load().uplift_la_last_kernel()
+
+
+def set_max_ctas(n: int) -> None:
+    """Cap the persistent tensor-core kernels at n CTAs (0: one per SM), so
+    that communication kernels running beside them get SMs of their own
+    (uplift_la_set_max_ctas)."""
+    check(load().uplift_la_set_max_ctas(int(n)), "uplift_la_set_max_ctas")
 
 
 def device_status(clear: bool = True) -> int:

@@ -682,7 +682,7 @@ int dl_tc_launch(const DlArgs& a, cudaStream_t stream) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (dev >= 0 && dev < 64) sm_count[dev].store(sms, std::memory_order_relaxed);
   }
-  const int grid = (int)std::min<int64_t>(nt, std::max(sms, 1));
+  const int grid = (int)std::min<int64_t>(nt, cta_budget(sms));
   return a.dtype == UPLIFT_LA_BF16 ? launch_k<__nv_bfloat16>(p, a.K, dev, grid, stream)
                                    : launch_k<__half>(p, a.K, dev, grid, stream);
 }

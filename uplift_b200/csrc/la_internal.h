@@ -60,6 +60,8 @@ int tcw_device_status(bool clear);
 // (uplift_la_set_host_status_word), or null; passed to every tensor-core
 // launch so that an expired wait is also written there.
 unsigned int* host_status_word();
+// CTAs for a persistent kernel: min(sms, the uplift_la_set_max_ctas limit), at least 1.
+int cta_budget(int sms);
 
 // Tensor-core dV of the backward (la_bwd_dv.cu): dvalue from dout and the
 // fp32 softmax workspace; strides in elements, channel stride 1 (NHWC).

@@ -963,7 +963,7 @@ int tc_launch(const TcArgs& a, cudaStream_t stream) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (dev >= 0 && dev < 64) sm_count[dev].store(sms, std::memory_order_relaxed);
   }
-  const int grid = (int)std::min<int64_t>(nt, std::max(sms, 1));
+  const int grid = (int)std::min<int64_t>(nt, cta_budget(sms));
   const bool gf = a.guide2 != nullptr;
   return a.dtype == UPLIFT_LA_BF16 ? launch_v<__nv_bfloat16>(p, a.K, rs, gf, dev, grid, stream)
                                    : launch_v<__half>(p, a.K, rs, gf, dev, grid, stream);

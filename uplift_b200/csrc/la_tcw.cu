@@ -521,7 +521,7 @@ int tcw_launch(const TcArgs& a, cudaStream_t stream) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (dev >= 0 && dev < 64) sm_count[dev].store(sms, std::memory_order_relaxed);
   }
-  const int grid = (int)std::min<int64_t>(nt, std::max(sms, 1));
+  const int grid = (int)std::min<int64_t>(nt, cta_budget(sms));
   switch (a.K) {
     case 5: return launch_t<5>(p, dev, grid, stream);
     case 9: return launch_t<9>(p, dev, grid, stream);

@@ -30,6 +30,14 @@ std::atomic<unsigned int*> g_host_status{nullptr};
 
 unsigned int* host_status_word() { return g_host_status.load(std::memory_order_acquire); }
 
+// CTA limit of the persistent tensor-core kernels (uplift_la_set_max_ctas; 0 = none).
+std::atomic<int> g_max_ctas{0};
+
+int cta_budget(int sms) {
+  const int l = g_max_ctas.load(std::memory_order_relaxed);
+  return std::max(1, (l > 0 && l < sms) ? l : sms);
+}
+
 int fail(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
@@ -446,6 +454,12 @@ int uplift_la_set_host_status_word(unsigned int* word) {
   return UPLIFT_LA_OK;
 }
 
+int uplift_la_set_max_ctas(int n) {
+  if (n < 0) return ula::fail(UPLIFT_LA_ERR_ARG, "uplift_la_set_max_ctas: n < 0");
+  ula::g_max_ctas.store(n, std::memory_order_relaxed);
+  return UPLIFT_LA_OK;
+}
+
 int uplift_la_test_hook(int fault, unsigned long long wait_limit_ns) {
   return ula::tc_set_test_hook(fault, wait_limit_ns);
 }
@@ -466,6 +480,6 @@ const char* uplift_la_status_string(int status) {
   }
 }
 
-int uplift_la_abi_version(void) { return (1 << 16) | 2; }
+int uplift_la_abi_version(void) { return (1 << 16) | 3; }
 
 }  // extern "C"
