@@ -862,11 +862,13 @@ def run_upsampler(dev, stream, world, rank, args, variant="dinov2-s14", img_px=1
     to last `min_ms`; img/s = global images / max-over-ranks time.
 
     `gather` (N > 1): a second timing in which every output also travels to
-    rank 0 (NCCL gather into one preallocated [global, C, H, W] tensor on
-    rank 0 only), micro-batch by micro-batch in `gather_micro_batch`-image
-    pieces so that the transfer of one overlaps the forward of the next
-    (two graph slots; a slot is replayed again only after its gather has
-    read it)."""
+    rank 0 into one preallocated [global, C, H, W] tensor held by rank 0
+    only, micro-batch by micro-batch so that the transfer of one overlaps the
+    forward of the next (two graph slots; a slot is replayed again only after
+    its transfer has read it).  By default the transfers are copy-engine
+    copies out of CUDA IPC mappings of the peers' slots (run_gather_ipc,
+    micro-batches of the forward's size); --gather-nccl uses NCCL's
+    dist.gather in `gather_micro_batch`-image pieces instead (run_gather)."""
     from uplift_b200.configs import get_config
     from uplift_b200.sharding import shard_bounds
     from uplift_b200.uplift import UPLiFT
@@ -942,9 +944,15 @@ def run_upsampler(dev, stream, world, rank, args, variant="dinov2-s14", img_px=1
 
         gat = None
         if gather and world > 1:
-            gat = run_gather(fast, dev, stream, world, rank, global_images, mine, lo, img, feats, size,
-                             dtype, out_shape, min(max(gather_micro_batch, getattr(args, "gather_groups", 1)), mb),
-                             timed, passes_for, getattr(args, "gather_ctas", 0), getattr(args, "gather_groups", 1))
+            nccl = getattr(args, "gather_nccl", False)
+            gather_micro_batch = getattr(args, "gather_mb", 0) or (gather_micro_batch if nccl else mb)
+            if not nccl:
+                gat = run_gather_ipc(fast, dev, stream, world, rank, global_images, mine, lo, img, feats, size,
+                                     dtype, out_shape, min(gather_micro_batch, mb), timed, passes_for)
+            else:
+                gat = run_gather(fast, dev, stream, world, rank, global_images, mine, lo, img, feats, size,
+                                 dtype, out_shape, min(max(gather_micro_batch, getattr(args, "gather_groups", 1)), mb),
+                                 timed, passes_for, getattr(args, "gather_ctas", 0), getattr(args, "gather_groups", 1))
     del fast, model, img, feats
     torch.cuda.empty_cache()
     dt = {torch.bfloat16: "bf16", torch.float32: "fp32"}[dtype]
@@ -1049,6 +1057,88 @@ def run_gather(fast, dev, stream, world, rank, global_images, mine, lo, img, fea
             "rank0_ingress_GB_s": round(into_root / (ms / 1e3) / 1e9, 1),
             "how": "NCCL gather per micro-batch into rank 0's [global, C, H, W] tensor, overlapping the next "
                    "micro-batch's forward (2 CUDA-graph slots); only rank 0 holds the full batch"}
+
+
+def run_gather_ipc(fast, dev, stream, world, rank, global_images, mine, lo, img, feats, size, dtype, out_shape,
+                   gmb, timed, passes_for):
+    """The gather of run_gather on the copy engines instead of NCCL
+    (uplift_b200.sharding.SlotGather): rank 0 maps every peer's two output
+    slots (the outputs of the two graphs) through CUDA IPC and copies each
+    micro-batch into its [global, C, H, W] tensor with cudaMemcpyAsync, one
+    stream per peer, while the ranks compute the next micro-batch; ordered
+    by interprocess events and TCPStore keys."""
+    import datetime
+    import torch.distributed as dist
+    from uplift_b200.sharding import SlotGather, shard_bounds
+    C, H, W = out_shape
+    bounds = [shard_bounds(global_images, r, world) for r in range(world)]
+    if len({hi - lo_ for lo_, hi in bounds}) != 1 or mine % gmb != 0:
+        return {"skipped": "unequal shards"}
+    port = int(os.environ.get("MASTER_PORT", "29500")) + 11
+    store = dist.TCPStore(os.environ.get("MASTER_ADDR", "127.0.0.1"), port, world, rank == 0,
+                          timeout=datetime.timedelta(seconds=60))
+    full = None
+    if rank == 0:
+        full = torch.empty((global_images, C, H, W), dtype=dtype, device=dev, memory_format=torch.channels_last)
+    n_mb = mine // gmb
+    x_img, x_feats = img[:gmb], feats[:gmb]
+    pool = torch.cuda.graph_pool_handle()
+    graphs, outs = [], []
+    for _ in range(2):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fast(x_img, x_feats, size)
+        stream.wait_stream(side)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, pool=pool):
+            outs.append(fast(x_img, x_feats, size))
+        graphs.append(gr)
+    torch.cuda.synchronize(dev)
+    torch.cuda.set_device(dev)
+    sg = SlotGather(outs, full, [b[0] for b in bounds], store, rank, world, stream)
+    counter = [0]  # micro-batches so far, across passes
+
+    def gather_pass():
+        for i in range(n_mb):
+            j = counter[0]
+            counter[0] += 1
+            sg.before_write(j)
+            graphs[j % 2].replay()
+            sg.after_write(j, i)
+        sg.join()
+    ok = True
+    try:
+        ms = timed(gather_pass, 1)
+        passes = passes_for(ms)
+        ms = timed(gather_pass, passes)
+        # check: every rank's last micro-batch, as copied, against an NCCL
+        # gather of the same slot
+        last = (counter[0] - 1) % 2
+        parts = [torch.empty_like(outs[last]) for _ in range(world)] if rank == 0 else None
+        dist.gather(outs[last].permute(0, 2, 3, 1), gather_list=None if parts is None else
+                    [t.permute(0, 2, 3, 1) for t in parts], dst=0)
+        if rank == 0:
+            for r in range(world):
+                lo_r = bounds[r][0]
+                ok &= bool(torch.equal(full[lo_r + (n_mb - 1) * gmb: lo_r + n_mb * gmb], parts[r]))
+    finally:
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        sg.close()
+        torch.cuda.synchronize(dev)
+        barrier(world)  # rank 0 has unmapped the peers' slots before they are freed
+    del graphs, outs, full, sg
+    elem = 2 if dtype != torch.float32 else 4
+    into_root = (world - 1) * mine * C * H * W * elem
+    return {"img_per_s": round(global_images / (ms / 1e3), 2), "ms_per_global_batch": round(ms, 2),
+            "passes": passes, "gather_micro_batch": gmb,
+            "bytes_into_rank0_per_batch": into_root,
+            "rank0_ingress_GB_s": round(into_root / (ms / 1e3) / 1e9, 1),
+            "last_micro_batch_equals_nccl_gather": ok,
+            "how": "uplift_b200.sharding.SlotGather: rank 0 copies each peer's micro-batch output out of its CUDA "
+                   "IPC mapping (cudaMemcpyAsync, one stream per peer), ordered by interprocess events, overlapping "
+                   "the next micro-batch's forward; only rank 0 holds the full batch"}
 
 
 def run_reference_upsampler(dev, stream, compile_model, images=16, micro_batch=8, min_ms=400.0):
@@ -1281,9 +1371,13 @@ def main():
     ap.add_argument("--only-fused-resize", action="store_true",
                     help="run only the fused attender + final resize timing (profiling captures; --images)")
     ap.add_argument("--gather-ctas", type=int, default=0,
-                    help="N>1: CTAs for the gather's own NCCL communicator, left free by the attender (0: none)")
+                    help="with --gather-nccl: CTAs for the gather's own communicator, left free by the attender")
     ap.add_argument("--gather-groups", type=int, default=1,
-                    help="N>1: concurrent NCCL communicators for the gather (one image per transfer)")
+                    help="with --gather-nccl: concurrent communicators (one image per transfer)")
+    ap.add_argument("--gather-mb", type=int, default=0,
+                    help="N>1: images per gathered micro-batch (0: the forward's micro-batch; 2 with --gather-nccl)")
+    ap.add_argument("--gather-nccl", action="store_true",
+                    help="N>1: gather with NCCL (dist.gather) instead of the copy engines through CUDA IPC")
     ap.add_argument("--no-ref-upsampler", action="store_true",
                     help="skip timing the reference's own compiled upsampler (N=1)")
     ap.add_argument("--only-reference-upsampler", action="store_true",

@@ -9,7 +9,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from uplift_b200.sharding import gather_to_rank0, shard, shard_bounds
+from uplift_b200.sharding import SlotGather, gather_to_rank0, shard, shard_bounds
 
 
 def test_shard_bounds_cover_in_order():
@@ -81,3 +81,13 @@ def test_failed_rank_is_detected_by_timeout():
     res = _run(2, 8, fail_rank=1)
     kinds = sorted(kind for kind, _ in res)
     assert kinds == ["err", "err"], res  # the failing rank and the one left waiting both end
+
+
+def test_slot_gather_rejects_host_and_mixed_slots():
+    """SlotGather (the copy-engine gather over CUDA IPC) validates its slots
+    before touching a device: host tensors and slots of different shapes are
+    refused."""
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        SlotGather([torch.zeros(2, 3), torch.zeros(2, 3)], None, [0, 2], None, 1, 2, None)
+    with pytest.raises(ValueError, match="one shape"):
+        SlotGather([torch.zeros(2, 3), torch.zeros(4, 3)], None, [0, 2], None, 1, 2, None)
