@@ -177,7 +177,9 @@ class SlotGather:
             return
         sl = j % self.n_slots
         if self.rank != 0:
-            self._store.wait([f"sg:d{self.rank}:{j - self.n_slots}"])
+            key = f"sg:d{self.rank}:{j - self.n_slots}"
+            self._store.wait([key])
+            self._store.delete_key(key)  # one key per event record: the store stays small
             self.stream.wait_event(self.peer_done[sl])
         else:
             self.stream.wait_event(self.done[0][sl])
@@ -198,6 +200,7 @@ class SlotGather:
         self.done[0][sl].record(cs)
         for r in range(1, self.world):
             self._store.wait([f"sg:r{r}:{j}"])
+            self._store.delete_key(f"sg:r{r}:{j}")
             cs = self.copy_streams[r]
             cs.wait_event(self.peer_ready[r][sl])
             lo = self.offsets[r] + index * self.items
