@@ -1074,9 +1074,15 @@ def run_gather_ipc(fast, dev, stream, world, rank, global_images, mine, lo, img,
     bounds = [shard_bounds(global_images, r, world) for r in range(world)]
     if len({hi - lo_ for lo_, hi in bounds}) != 1 or mine % gmb != 0:
         return {"skipped": "unequal shards"}
-    port = int(os.environ.get("MASTER_PORT", "29500")) + 11
-    store = dist.TCPStore(os.environ.get("MASTER_ADDR", "127.0.0.1"), port, world, rank == 0,
-                          timeout=datetime.timedelta(seconds=60))
+    # the process group's own rendezvous store (no second port to open),
+    # under a prefix of this gather's own; a new TCPStore only without one
+    try:
+        from torch.distributed.distributed_c10d import _get_default_store
+        store = dist.PrefixStore("slotgather/", _get_default_store())
+    except Exception:  # noqa: BLE001 -- no default store: open one beside the rendezvous port
+        port = int(os.environ.get("MASTER_PORT", "29500")) + 11
+        store = dist.TCPStore(os.environ.get("MASTER_ADDR", "127.0.0.1"), port, world, rank == 0)
+    store.set_timeout(datetime.timedelta(seconds=60))
     full = None
     if rank == 0:
         full = torch.empty((global_images, C, H, W), dtype=dtype, device=dev, memory_format=torch.channels_last)
