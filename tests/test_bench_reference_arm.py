@@ -29,3 +29,19 @@ def test_reference_arm_json_line():
     sys.path.insert(0, str(ROOT))
     import bench
     assert d["config"] == bench.workload_config(1)  # the repository arm's config object
+
+
+def test_summary_tolerates_missing_legs():
+    """The short `summary` key at the end of the bench line carries the
+    headline figures even when legs were skipped (N > 1 skips the reference
+    upsampler and the CPU baseline; --no-* flags skip others): absent legs
+    read as None instead of failing the line."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    r = {"n_gpus": 2, "value": 10000.0, "roofline": {"frac": 0.88},
+         "upsampler": {"img_per_s": 540.0, "gather": {"img_per_s": 500.0}}}
+    s = bench.summary(r)
+    assert s["n"] == 2 and s["attender_Mpix_s"] == 10000.0 and s["frac"] == 0.88
+    assert s["cfg5_img_s"] == 540.0 and s["cfg5_img_s_gather"] == 500.0
+    for key in ("e2e_Mpix_s", "triton_ref_Mpix_s", "cfg5_ref_compiled_img_s", "cfg3_img_s", "bwd_frac"):
+        assert s[key] is None, key
